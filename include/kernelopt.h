@@ -1,0 +1,142 @@
+/*
+ * kernelopt.h — C ABI of libkernelopt.so, the sm_100a (B200) kernels of the RF-DETR-Medium inference hot path.
+ *
+ * The reference (ishaanzee/kernelopt) reaches its four GPU kernels through Python wrappers around
+ * mx.fast.metal_kernel in fast_rfdetr/kernels.py. Each entry point below replaces one of those wrappers (or the
+ * host helper it relies on); the comment on each cites the reference interface it stands in for.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor arguments are raw device pointers to contiguous, row-major buffers owned by the caller.
+ *     No entry point allocates device memory; scratch space, where needed, is passed in by the caller.
+ *   - Sizes are int64_t. Scalars (eps, mode, offset) are passed by value.
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream). Work is enqueued asynchronously.
+ *   - The return value is KO_OK (0), a cudaError_t value (1..999) from a failed launch, or one of the KO_ERR_*
+ *     codes below. ko_last_error_string() describes the most recent failure on the calling host thread.
+ *   - Kernels that wait on on-chip barriers (the tcgen05 GEMM) bound every wait. When a wait runs out the
+ *     kernel writes KO_ERR_DEVICE_TIMEOUT into *dev_status (an int in device memory, may be NULL) and returns;
+ *     the caller reads it after synchronising.
+ */
+#ifndef KERNELOPT_H_
+#define KERNELOPT_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* ko_stream_t; /* identical to cudaStream_t */
+
+#define KO_OK 0
+#define KO_ERR_INVALID_ARGUMENT 1001 /* a size, layout or alignment precondition does not hold */
+#define KO_ERR_UNSUPPORTED 1002      /* the device is not sm_100 or a driver entry point is missing */
+#define KO_ERR_DEVICE_TIMEOUT 1003   /* written to *dev_status by a kernel whose bounded wait ran out */
+
+/* Output layouts of ko_preprocess / ko_preprocess_batch. */
+#define KO_LAYOUT_HWC 0     /* [dst, dst, 3] RGB, the reference's preprocess_gpu output */
+#define KO_LAYOUT_CHW 1     /* [3, dst, dst] RGB, the NCHW tensor Ballform's cv2 path produces */
+#define KO_LAYOUT_PATCH16 2 /* [(dst/16)^2, 16*16*3]: 16x16 patches flattened as (ky, kx, c) — the im2col of the
+                               ViT patch-embedding convolution, so that convolution becomes one GEMM */
+
+/* Table policies of ko_resize_tables. */
+#define KO_RESIZE_REFERENCE 0 /* the reference's model of the macOS arm64 cv2 wheel: KleidiCV arithmetic for the
+                                 sizes that wheel hands to KleidiCV, OpenCV's fixed-point arithmetic otherwise */
+#define KO_RESIZE_OPENCV 1    /* OpenCV's own fixed-point path for every size: cv2 builds without KleidiCV,
+                                 such as the x86-64 wheels */
+
+/* Activations of ko_linear_f32_packed. */
+#define KO_ACT_NONE 0
+#define KO_ACT_GELU 1 /* exact erf GELU: 0.5 v (1 + erf(v / sqrt 2)) */
+#define KO_ACT_RELU 2
+
+/* --- status / version ------------------------------------------------------------------------------------- */
+
+/* Text of the last failure on the calling host thread ("" if none). */
+const char* ko_last_error_string(void);
+/* ABI version, bumped whenever a signature below changes. */
+int ko_abi_version(void);
+/* 0 when the current device is an sm_100-class GPU this library was built for, else KO_ERR_UNSUPPORTED. */
+int ko_check_device(void);
+
+/* --- preprocessing: uint8 BGR frame -> resized, RGB, normalised float32 ------------------------------------ */
+
+/* Host function. Fills the interpolation tables that reproduce cv2.resize(INTER_LINEAR) of a uint8 3-channel
+ * image from src_w x src_h to dst_w x dst_h. Replaces resize_tables.tables (fast_rfdetr/resize_tables.py:165-184).
+ *   xtab: int32 [dst_w*3][4] = (left element, right element, weight a, weight b) per output element x*3+c
+ *   ytab: int32 [dst_h][4]   = (top row, bottom row, weight a, weight b) per output row
+ *   *mode: 0 = KleidiCV arithmetic, 1 = OpenCV arithmetic (the `mode` argument of ko_preprocess). */
+int ko_resize_tables(int64_t src_w, int64_t src_h, int64_t dst_w, int64_t dst_h, int policy, int32_t* xtab,
+                     int32_t* ytab, int* mode);
+
+/* One frame. Replaces preprocess_gpu (fast_rfdetr/kernels.py:106-116; kernel source :74-103).
+ * src: uint8 [src_h][src_stride] holding BGR pixels (src_stride >= src_w*3 bytes); xtab/ytab from
+ * ko_resize_tables (device copies); lut: float32 [3][256] with lut[c][v] = (v/255 - mean[c]) / std[c] for RGB
+ * channel c; out: float32 in `layout`. Output is bit-identical to the reference kernel on the same tables. */
+int ko_preprocess(const uint8_t* src, int64_t src_h, int64_t src_w, int64_t src_stride, const int32_t* xtab,
+                  const int32_t* ytab, const float* lut, int mode, int64_t dst, int layout, float* out,
+                  ko_stream_t stream);
+
+/* One image of a batch for ko_preprocess_batch (all pointers are device pointers). */
+typedef struct ko_image_desc {
+  const uint8_t* src;
+  const int32_t* xtab;
+  const int32_t* ytab;
+  int64_t src_h, src_w, src_stride;
+  int32_t mode;
+  int32_t _pad;
+} ko_image_desc;
+
+/* Several frames of any sizes in one launch; image i is written at out + i*dst*dst*3. Replaces the per-image
+ * preprocess_gpu loop of FastBasketballDetector.raw_batch (fast_rfdetr/detector.py:100). `images` is a HOST
+ * array of n descriptors; n <= 64 per call. */
+int ko_preprocess_batch(const ko_image_desc* images, int n, const float* lut, int64_t dst, int layout, float* out,
+                        ko_stream_t stream);
+
+/* --- fused residual add + LayerNorm ------------------------------------------------------------------------- */
+
+/* h_out = h + (o + bias) * scale;  y = (h_out - mean) / sqrt(var + eps) * gamma + beta  (row statistics in fp32,
+ * biased variance). h, o, h_out, y: float32 [rows][C]; bias, scale, gamma, beta: float32 [C]. C % 4 == 0.
+ * bias and scale may be NULL (0 and 1). h_out may alias h. Replaces residual_layernorm
+ * (fast_rfdetr/kernels.py:53-67; kernel source :9-48). */
+int ko_residual_layernorm(const float* h, const float* o, const float* bias, const float* scale, const float* gamma,
+                          const float* beta, float eps, int64_t rows, int64_t C, float* h_out, float* y,
+                          ko_stream_t stream);
+
+/* --- deformable-attention sampling (single level) ----------------------------------------------------------- */
+
+/* out[b,q,h*HD+d] = sum_p aw[b,q,h,p] * bilinear(value[b, :, offset + h*HD + d] viewed as GH x GW, loc[b,q,h,p])
+ * with grid_sample semantics (align_corners=False, zero padding): x = loc_x*GW - 0.5, y = loc_y*GH - 0.5.
+ * value: float32 [B][GH*GW][ROW]; loc: float32 [B][NQ][NH][NP][2] (x, y in [0,1]); aw: float32 [B][NQ][NH][NP];
+ * out: float32 [B][NQ][NH*HD]. offset + NH*HD <= ROW. Replaces deform_attn (fast_rfdetr/kernels.py:165-181;
+ * kernel source :124-162). */
+int ko_deform_attn(const float* value, const float* loc, const float* aw, int64_t B, int64_t NQ, int64_t NH,
+                   int64_t HD, int64_t NP, int64_t GH, int64_t GW, int64_t ROW, int64_t offset, float* out,
+                   ko_stream_t stream);
+
+/* --- fp32-grade GEMM on tcgen05 tensor cores (3xTF32 split) ------------------------------------------------- */
+
+/* Bytes of scratch that ko_linear_gelu_f32 needs for a [K, N] weight (its split, transposed copy). */
+int64_t ko_linear_workspace_bytes(int64_t K, int64_t N);
+
+/* Splits w (float32 [K][N], the x @ W convention) into w_packed = float32 [2][N][K]: w_packed[0] = tf32(w)^T,
+ * w_packed[1] = tf32(w - tf32(w))^T. Run once per weight; the result feeds ko_linear_f32_packed. No reference
+ * counterpart (the reference's GEMM reads w directly, fast_rfdetr/kernels.py:245). */
+int ko_pack_weight_tf32x3(const float* w, int64_t K, int64_t N, float* w_packed, ko_stream_t stream);
+
+/* out = act(x @ W + bias) with x float32 [M][K], W given pre-split by ko_pack_weight_tf32x3, bias float32 [N]
+ * (may be NULL), out float32 [M][N]. Three TF32 tensor-core products (hi*hi + hi*lo + lo*hi) with fp32
+ * accumulation in TMEM give fp32-grade results. K % 4 == 0, N % 4 == 0, 16-byte aligned pointers. */
+int ko_linear_f32_packed(const float* x, const float* w_packed, const float* bias, int64_t M, int64_t K, int64_t N,
+                         int act, float* out, int* dev_status, ko_stream_t stream);
+
+/* out = GELU_erf(x @ w + bias): packs w into `workspace` (ko_linear_workspace_bytes(K, N) bytes, 16-byte
+ * aligned) and runs ko_linear_f32_packed. Replaces linear_gelu_f32 (fast_rfdetr/kernels.py:271-285; kernel
+ * source :188-266). */
+int ko_linear_gelu_f32(const float* x, const float* w, const float* bias, int64_t M, int64_t K, int64_t N,
+                       float* out, void* workspace, int64_t workspace_bytes, int* dev_status, ko_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KERNELOPT_H_ */

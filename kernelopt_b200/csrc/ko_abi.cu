@@ -1,0 +1,96 @@
+// Status reporting, device checks and tensor-map encoding shared by all entry points of libkernelopt.
+#include <cstdio>
+#include <mutex>
+#include <vector>
+
+#include "ko_common.cuh"
+
+namespace ko {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return static_cast<int>(e);
+  }
+  return KO_OK;
+}
+
+const DeviceInfo& device_info() {
+  static std::mutex mu;
+  static std::vector<DeviceInfo> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1);
+  DeviceInfo& d = cache[dev];
+  if (d.sm_count == 0) {
+    cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
+  }
+  return d;
+}
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                     uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swizzle, const char* what) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(KO_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled is not available from the driver");
+  if (!aligned16(base) || (pitch_elems * 4) % 16 != 0)
+    return fail(KO_ERR_INVALID_ARGUMENT, std::string(what) + ": base must be 16-byte aligned and the row pitch a "
+                                                             "multiple of 16 bytes");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_elems * 4};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[160];
+    snprintf(buf, sizeof buf, "%s: cuTensorMapEncodeTiled failed (CUresult %d)", what, static_cast<int>(r));
+    return fail(KO_ERR_INVALID_ARGUMENT, buf);
+  }
+  return KO_OK;
+}
+
+}  // namespace ko
+
+extern "C" {
+
+const char* ko_last_error_string(void) { return ko::g_last_error.c_str(); }
+
+int ko_abi_version(void) { return 1; }
+
+int ko_check_device(void) {
+  const ko::DeviceInfo& d = ko::device_info();
+  if (d.major != 10)
+    return ko::fail(KO_ERR_UNSUPPORTED, "libkernelopt is built for sm_100a (B200); current device is sm_" +
+                                            std::to_string(d.major) + std::to_string(d.minor));
+  return KO_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,137 @@
+// Deformable-attention bilinear sampling with the attention-weighted sum over points (single feature level).
+//
+// Semantics: the reference kernel fast_rfdetr/kernels.py:124-162 (deform_attn_sample) and the unfused form
+// model.py:196-216 + 228-229, i.e. ONNX GridSample (bilinear, zero padding, align_corners=False) on the grid
+// 2*loc - 1, then sum_p aw * sample:
+//   x = loc_x * GW - 0.5, y = loc_y * GH - 0.5, x0 = floor(x), fx = x - x0 (same for y); taps outside the
+//   GH x GW map contribute 0; s_p = sum over the 4 taps of w_x * w_y * value; out = sum_p aw_p * s_p.
+//
+// B200 design. The value map of one frame and layer is 40x40 tokens x 256 channels (1.6 MB) — too large for
+// shared memory, but the whole batch of maps stays resident in the 126 MB L2 while it is sampled. Four lanes
+// serve one (query, head): each lane owns 4 of the head's 16 channels, so a tap is one 64-byte contiguous read
+// by a lane quad (128-bit loads, 2 full sectors), the quad's sampling coordinates are broadcast loads, and the
+// output of a warp (8 heads x 64 bytes) is one contiguous 512-byte store. A scalar kernel covers head sizes or
+// column offsets that are not multiples of 4.
+#include "ko_common.cuh"
+
+namespace {
+
+struct DeformShape {
+  int64_t B, NQ, NH, HD, NP, GH, GW, ROW, offset;
+};
+
+__device__ __forceinline__ void fma4(float4& acc, float w, const float4& v) {
+  acc.x += w * v.x;
+  acc.y += w * v.y;
+  acc.z += w * v.z;
+  acc.w += w * v.w;
+}
+
+// One thread per (b, q, h, 4-channel group).
+__global__ void __launch_bounds__(256) deform_vec4_kernel(const float* __restrict__ value,
+                                                          const float* __restrict__ loc,
+                                                          const float* __restrict__ aw, DeformShape s,
+                                                          float* __restrict__ out) {
+  const int64_t groups = s.HD >> 2;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = s.B * s.NQ * s.NH * groups;
+  if (t >= total) return;
+  const int64_t g = t % groups;
+  const int64_t qh = t / groups;            // (b*NQ + q)*NH + h
+  const int64_t h = qh % s.NH;
+  const int64_t b = qh / (s.NH * s.NQ);
+  const int GW = static_cast<int>(s.GW), GH = static_cast<int>(s.GH);
+  const float* vb = value + b * (s.GH * s.GW * s.ROW) + s.offset + h * s.HD + g * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int p = 0; p < s.NP; ++p) {
+    const int64_t li = qh * s.NP + p;
+    const float2 lxy = __ldg(reinterpret_cast<const float2*>(loc) + li);
+    const float lx = lxy.x * static_cast<float>(GW) - 0.5f;
+    const float ly = lxy.y * static_cast<float>(GH) - 0.5f;
+    const float x0f = floorf(lx), y0f = floorf(ly);
+    const float fx = lx - x0f, fy = ly - y0f;
+    const int x0 = static_cast<int>(x0f), y0 = static_cast<int>(y0f);
+    const float w = __ldg(aw + li);
+    float4 sacc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int dy = 0; dy < 2; ++dy) {
+      const int yy = y0 + dy;
+      if (yy < 0 || yy >= GH) continue;
+      const float wy = dy ? fy : 1.0f - fy;
+#pragma unroll
+      for (int dx = 0; dx < 2; ++dx) {
+        const int xx = x0 + dx;
+        if (xx < 0 || xx >= GW) continue;
+        const float wx = dx ? fx : 1.0f - fx;
+        const float4 v = __ldg(reinterpret_cast<const float4*>(vb + static_cast<int64_t>(yy * GW + xx) * s.ROW));
+        fma4(sacc, wx * wy, v);
+      }
+    }
+    fma4(acc, w, sacc);
+  }
+  reinterpret_cast<float4*>(out)[t] = acc;
+}
+
+// General layout: one thread per (b, q, h, d).
+__global__ void __launch_bounds__(256) deform_scalar_kernel(const float* __restrict__ value,
+                                                            const float* __restrict__ loc,
+                                                            const float* __restrict__ aw, DeformShape s,
+                                                            float* __restrict__ out) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = s.B * s.NQ * s.NH * s.HD;
+  if (t >= total) return;
+  const int64_t d = t % s.HD;
+  const int64_t qh = t / s.HD;
+  const int64_t h = qh % s.NH;
+  const int64_t b = qh / (s.NH * s.NQ);
+  const int GW = static_cast<int>(s.GW), GH = static_cast<int>(s.GH);
+  const float* vb = value + b * (s.GH * s.GW * s.ROW) + s.offset + h * s.HD + d;
+  float acc = 0.f;
+  for (int p = 0; p < s.NP; ++p) {
+    const int64_t li = qh * s.NP + p;
+    const float lx = __ldg(loc + li * 2) * static_cast<float>(GW) - 0.5f;
+    const float ly = __ldg(loc + li * 2 + 1) * static_cast<float>(GH) - 0.5f;
+    const float x0f = floorf(lx), y0f = floorf(ly);
+    const float fx = lx - x0f, fy = ly - y0f;
+    const int x0 = static_cast<int>(x0f), y0 = static_cast<int>(y0f);
+    float sacc = 0.f;
+    for (int dy = 0; dy < 2; ++dy) {
+      const int yy = y0 + dy;
+      if (yy < 0 || yy >= GH) continue;
+      const float wy = dy ? fy : 1.0f - fy;
+      for (int dx = 0; dx < 2; ++dx) {
+        const int xx = x0 + dx;
+        if (xx < 0 || xx >= GW) continue;
+        const float wx = dx ? fx : 1.0f - fx;
+        sacc += wx * wy * __ldg(vb + static_cast<int64_t>(yy * GW + xx) * s.ROW);
+      }
+    }
+    acc += __ldg(aw + li) * sacc;
+  }
+  out[t] = acc;
+}
+
+}  // namespace
+
+extern "C" int ko_deform_attn(const float* value, const float* loc, const float* aw, int64_t B, int64_t NQ,
+                              int64_t NH, int64_t HD, int64_t NP, int64_t GH, int64_t GW, int64_t ROW,
+                              int64_t offset, float* out, ko_stream_t stream) {
+  if (B < 0 || NQ < 0 || NH < 1 || HD < 1 || NP < 1 || GH < 1 || GW < 1 || offset < 0 || offset + NH * HD > ROW)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_deform_attn: bad shape (need offset + NH*HD <= ROW)");
+  if (GH * GW > (int64_t(1) << 30) / 1) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_deform_attn: map too large");
+  if (B == 0 || NQ == 0) return KO_OK;
+  if (!value || !loc || !aw || !out) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_deform_attn: null pointer");
+  if ((reinterpret_cast<uintptr_t>(loc) & 7) != 0)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_deform_attn: loc must be 8-byte aligned");
+  DeformShape s{B, NQ, NH, HD, NP, GH, GW, ROW, offset};
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool vec = HD % 4 == 0 && offset % 4 == 0 && ROW % 4 == 0 && ko::aligned16(value) && ko::aligned16(out);
+  const int64_t total = B * NQ * NH * (vec ? HD / 4 : HD);
+  const int64_t blocks = (total + 255) / 256;
+  if (blocks > 0x7fffffff) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_deform_attn: problem too large");
+  if (vec)
+    deform_vec4_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(value, loc, aw, s, out);
+  else
+    deform_scalar_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(value, loc, aw, s, out);
+  return ko::check_launch("ko_deform_attn");
+}

@@ -1,0 +1,477 @@
+// fp32-grade GEMM with fused bias + activation on the B200 5th-generation tensor cores (tcgen05, kind::tf32).
+//
+//   out[M][N] = act(x[M][K] @ W[K][N] + bias[N])
+//
+// Semantics: the reference's fused fc1 kernel fast_rfdetr/kernels.py:188-266 (gemm_bias_gelu_f32, with the
+// exact-erf GELU epilogue) and its unfused form model.py:142-143 (lin + 0.5*y*(1+erf(y/sqrt 2))).
+//
+// Precision: 3xTF32 (the error-compensated split of Ootomo & Yokota, 2022, also known as CUTLASS "3xTF32").
+// Every operand is split as v = hi + lo with hi = tf32_rn(v) and lo = tf32_rn(v - hi); the tensor cores
+// accumulate hi*hi + hi*lo + lo*hi in fp32 in tensor memory, which leaves an error of about 2^-21 relative per
+// product — the same order as a plain fp32 dot product of this length. The weight split is done once
+// (ko_pack_weight_tf32x3); the activation split happens on chip, inside the pipeline, from the fp32 tile that
+// TMA brought in, so x is read from HBM exactly once.
+//
+// Kernel structure (persistent, one CTA per SM, 320 threads, warp-specialised):
+//   warp 0      TMA producer: x tile [128 x 32] and W_hi/W_lo tiles [BN x 32] per k-block, 128-byte swizzle
+//   warp 1      allocates TMEM; one lane issues the tcgen05.mma (12 per k-block: 4 k-steps x 3 products)
+//   warps 2-5   split the x tile in shared memory: hi in place, lo into a second buffer (same layout)
+//   warps 6-9   epilogue: TMEM -> registers (tcgen05.ld), + bias, activation, 128-bit stores
+// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the MMAs of tile i+1.
+// Every wait on an mbarrier is bounded (2 s); on timeout the CTA stops, drains what it issued, frees TMEM and
+// reports KO_ERR_DEVICE_TIMEOUT through dev_status.
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+
+#include "ko_common.cuh"
+
+namespace {
+
+using namespace kodev;
+
+constexpr int BM = 128;
+constexpr int kThreads = 320;
+constexpr int kTransformWarp0 = 2;
+constexpr int kEpilogueWarp0 = 6;
+constexpr size_t kSmemBudget = 224 * 1024;  // stage buffers; barriers and alignment slack come on top
+
+// BN: tile width (MMA N). BKB: bytes of K per k-block row (128 -> 128-byte swizzle, 64 -> 64-byte swizzle).
+// SPLIT: accumulate the small hi*lo + lo*hi terms in their own TMEM accumulator and add it to the hi*hi
+// accumulator in the epilogue. The tensor core's fp32 accumulation drops low-order bits at every MMA; with a
+// single accumulator the 2 x K/8 correction MMAs land on a large running sum, which makes the error grow with
+// K. With SPLIT they land on a small one, and the large sum sees only K/8 additions.
+template <int BN, int BKB, bool SPLIT>
+struct Cfg {
+  static constexpr int kBK = BKB / 4;                       // fp32 elements per k-block
+  static constexpr uint32_t kATileBytes = BM * BKB;
+  static constexpr uint32_t kBTileBytes = BN * BKB;
+  static constexpr uint32_t kStageBytes = 2 * kATileBytes + 2 * kBTileBytes;
+  static constexpr int kStagesRaw = static_cast<int>(kSmemBudget / kStageBytes);
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static constexpr uint32_t kAccCols = BN * (SPLIT ? 2 : 1);  // TMEM columns of one tile's accumulator(s)
+  static constexpr int kAccBufs = (2 * kAccCols <= 512) ? 2 : 1;
+  static constexpr uint32_t kTmemNeed = kAccBufs * kAccCols;
+  static constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
+                                        : kTmemNeed <= 256 ? 256 : 512;
+  static constexpr uint32_t kTxBytes = kATileBytes + 2 * kBTileBytes;
+  static constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + 256 /*barriers*/;
+  static constexpr uint32_t kSbo = 8 * BKB;                 // bytes between 8-row groups
+  static constexpr uint32_t kLayout = BKB == 128 ? 2u : 4u;  // descriptor layout: 128B / 64B swizzle
+  static_assert(kStages >= 2, "stage does not fit");
+  static_assert(kAccCols * kAccBufs <= 512, "TMEM overflow");
+};
+
+struct GemmArgs {
+  const float* bias;
+  float* out;
+  int* dev_status;
+  int M, N, K, act;
+  int m_tiles, n_tiles, k_blocks;
+};
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  if (act == KO_ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
+  if (act == KO_ACT_RELU) return fmaxf(v, 0.0f);
+  return v;
+}
+
+// K-major operand descriptor for a swizzled tile (see smem_desc_k_sw128 for the field layout).
+template <uint32_t kLayout, uint32_t kSbo>
+__device__ __forceinline__ uint64_t desc_k(uint32_t addr) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1u) << 16) |
+         (static_cast<uint64_t>((kSbo >> 4) & 0x3FFFu) << 32) | (static_cast<uint64_t>(1u) << 46) |
+         (static_cast<uint64_t>(kLayout) << 61);
+}
+
+template <int BN, int BKB, bool SPLIT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_whi,
+                       const __grid_constant__ CUtensorMap map_wlo, const GemmArgs args) {
+  using C = Cfg<BN, BKB, SPLIT>;
+  constexpr int S = C::kStages;
+  constexpr int NB = C::kAccBufs;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // stage st: [x -> hi][lo][W_hi][W_lo]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
+  uint64_t* full = bars;               // TMA landed            (1 arrival + tx bytes)
+  uint64_t* ready = bars + S;          // x split done          (4 arrivals)
+  uint64_t* empty = bars + 2 * S;      // MMAs of stage done    (1 commit)
+  uint64_t* acc_full = bars + 3 * S;   // accumulator complete  (1 commit) x NB
+  uint64_t* acc_empty = acc_full + 2;  // accumulator drained   (4 arrivals) x NB
+  uint64_t* mma_done = acc_empty + 2;  // teardown drain        (1 commit)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = args.m_tiles * args.n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&map_x);
+    prefetch_tmap(&map_whi);
+    prefetch_tmap(&map_wlo);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t issued[S];
+#pragma unroll
+      for (int s = 0; s < S; ++s) issued[s] = 0;
+      int st = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / args.n_tiles) * BM, n0 = (tile % args.n_tiles) * BN;
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[st], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sbase = smem + st * C::kStageBytes;
+          mbar_arrive_expect_tx(&full[st], C::kTxBytes);
+          tma_load_2d(&map_x, &full[st], sbase, kb * C::kBK, m0);
+          tma_load_2d(&map_whi, &full[st], sbase + 2 * C::kATileBytes, kb * C::kBK, n0);
+          tma_load_2d(&map_wlo, &full[st], sbase + 2 * C::kATileBytes + C::kBTileBytes, kb * C::kBK, n0);
+#pragma unroll
+          for (int s = 0; s < S; ++s) issued[s] += (s == st);
+          if (++st == S) {
+            st = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: every load this thread issued must have landed before the CTA may exit.
+#pragma unroll
+      for (int s = 0; s < S; ++s) {
+        if (issued[s] == 0) continue;
+        volatile int never = 0;
+        if (!mbar_wait(&full[s], (issued[s] - 1) & 1u, &never)) *abort_flag = 1;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(BM, BN);
+      int st = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      const uint32_t sb = smem_addr(smem);
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int as = local % NB;
+        const uint32_t acc_phase = (local / NB) & 1u;
+        if (!mbar_wait(&acc_empty[as], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_main = tmem_base + as * C::kAccCols;
+        const uint32_t d_corr = SPLIT ? d_main + BN : d_main;
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!mbar_wait(&ready[st], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_hi = sb + st * C::kStageBytes;
+          const uint32_t a_lo = a_hi + C::kATileBytes;
+          const uint32_t b_hi = a_hi + 2 * C::kATileBytes;
+          const uint32_t b_lo = b_hi + C::kBTileBytes;
+#pragma unroll
+          for (int k = 0; k < C::kBK / 8; ++k) {
+            const uint32_t koff = k * 32;  // 8 tf32 = 32 bytes along the swizzled row
+            const uint32_t first = (kb == 0 && k == 0) ? 0u : 1u;
+            mma_tf32(d_corr, desc_k<C::kLayout, C::kSbo>(a_lo + koff), desc_k<C::kLayout, C::kSbo>(b_hi + koff),
+                     idesc, first);
+            mma_tf32(d_corr, desc_k<C::kLayout, C::kSbo>(a_hi + koff), desc_k<C::kLayout, C::kSbo>(b_lo + koff),
+                     idesc, 1u);
+            mma_tf32(d_main, desc_k<C::kLayout, C::kSbo>(a_hi + koff), desc_k<C::kLayout, C::kSbo>(b_hi + koff),
+                     idesc, SPLIT ? first : 1u);
+          }
+          mma_commit(&empty[st]);
+          if (++st == S) {
+            st = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[as]);
+      }
+      // Drain: wait for every MMA this thread issued before TMEM is released.
+      mma_commit(mma_done);
+      volatile int never = 0;
+      if (!mbar_wait(mma_done, 0, &never)) *abort_flag = 1;
+    }
+  } else if (warp < kEpilogueWarp0) {
+    // ---------------- x split: hi in place, lo alongside ----------------
+    const int t = threadIdx.x - kTransformWarp0 * 32;  // 0..127
+    int st = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int kb = 0; kb < args.k_blocks; ++kb) {
+        if (!mbar_wait(&full[st], phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        float4* xa = reinterpret_cast<float4*>(smem + st * C::kStageBytes);
+        float4* xl = reinterpret_cast<float4*>(smem + st * C::kStageBytes + C::kATileBytes);
+#pragma unroll
+        for (int i = 0; i < static_cast<int>(C::kATileBytes / 16 / 128); ++i) {
+          const int idx = t + i * 128;
+          const float4 v = xa[idx];
+          float4 hi, lo;
+          hi.x = __uint_as_float(f32_to_tf32_rna(v.x));
+          hi.y = __uint_as_float(f32_to_tf32_rna(v.y));
+          hi.z = __uint_as_float(f32_to_tf32_rna(v.z));
+          hi.w = __uint_as_float(f32_to_tf32_rna(v.w));
+          lo.x = __uint_as_float(f32_to_tf32_rna(v.x - hi.x));
+          lo.y = __uint_as_float(f32_to_tf32_rna(v.y - hi.y));
+          lo.z = __uint_as_float(f32_to_tf32_rna(v.z - hi.z));
+          lo.w = __uint_as_float(f32_to_tf32_rna(v.w - hi.w));
+          xa[idx] = hi;
+          xl[idx] = lo;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[st]);
+        if (++st == S) {
+          st = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int as = local % NB;
+      const uint32_t acc_phase = (local / NB) & 1u;
+      if (!mbar_wait(&acc_full[as], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int m0 = (tile / args.n_tiles) * BM, n0 = (tile % args.n_tiles) * BN;
+      const int row = m0 + row_in_tile;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + as * C::kAccCols;
+      float* orow = args.out + static_cast<int64_t>(row) * args.N;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_ld_wait_regs(r);
+        if constexpr (SPLIT) {
+          uint32_t q[32];
+          tmem_ld_32x32b_x32(taddr + BN + c * 32, q);
+          tmem_ld_wait_regs(q);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
+        }
+        if (c == BN / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[as]);
+        }
+        const int col0 = n0 + c * 32;
+        if (row < args.M) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const int col = col0 + j;
+            if (col < args.N) {
+              float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (args.bias) b = __ldg(reinterpret_cast<const float4*>(args.bias + col));
+              float4 o;
+              o.x = apply_act(__uint_as_float(r[j + 0]) + b.x, args.act);
+              o.y = apply_act(__uint_as_float(r[j + 1]) + b.y, args.act);
+              o.z = apply_act(__uint_as_float(r[j + 2]) + b.z, args.act);
+              o.w = apply_act(__uint_as_float(r[j + 3]) + b.w, args.act);
+              *reinterpret_cast<float4*>(orow + col) = o;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag && args.dev_status) atomicExch(args.dev_status, KO_ERR_DEVICE_TIMEOUT);
+}
+
+// W[K][N] -> packed[2][N][K] (hi = tf32_rn(w), lo = tf32_rn(w - hi)), transposed through a 32x32 tile.
+__global__ void __launch_bounds__(256) pack_weight_kernel(const float* __restrict__ w, int K, int N,
+                                                          float* __restrict__ packed) {
+  __shared__ float tile[32][33];
+  const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int k = k0 + i, n = n0 + threadIdx.x;
+    tile[i][threadIdx.x] = (k < K && n < N) ? w[static_cast<int64_t>(k) * N + n] : 0.f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int n = n0 + i, k = k0 + threadIdx.x;
+    if (n < N && k < K) {
+      const float v = tile[threadIdx.x][i];
+      const float hi = __uint_as_float(kodev::f32_to_tf32_rna(v));
+      const float lo = __uint_as_float(kodev::f32_to_tf32_rna(v - hi));
+      packed[static_cast<int64_t>(n) * K + k] = hi;
+      packed[static_cast<int64_t>(N) * K + static_cast<int64_t>(n) * K + k] = lo;
+    }
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------------------------
+namespace {
+
+template <int BN, int BKB, bool SPLIT>
+int launch_gemm(const float* x, const float* w_packed, const float* bias, int64_t M, int64_t K, int64_t N,
+                int act, float* out, int* dev_status, cudaStream_t stream) {
+  using C = Cfg<BN, BKB, SPLIT>;
+  const CUtensorMapSwizzle sw = BKB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUtensorMap mx, mhi, mlo;
+  int st = ko::make_tmap_2d_f32(&mx, x, M, K, K, BM, C::kBK, sw, "ko_linear x");
+  if (st) return st;
+  st = ko::make_tmap_2d_f32(&mhi, w_packed, N, K, K, BN, C::kBK, sw, "ko_linear w_hi");
+  if (st) return st;
+  st = ko::make_tmap_2d_f32(&mlo, w_packed + N * K, N, K, K, BN, C::kBK, sw, "ko_linear w_lo");
+  if (st) return st;
+  const ko::DeviceInfo& info = ko::device_info();
+  if (static_cast<int64_t>(C::kSmemBytes) > info.max_smem_optin)
+    return ko::fail(KO_ERR_UNSUPPORTED, "ko_linear: not enough shared memory on this device");
+  cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BKB, SPLIT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmemBytes));
+  if (e != cudaSuccess) return ko::fail(static_cast<int>(e), "ko_linear: cudaFuncSetAttribute failed");
+  GemmArgs a;
+  a.bias = bias;
+  a.out = out;
+  a.dev_status = dev_status;
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.act = act;
+  a.m_tiles = static_cast<int>((M + BM - 1) / BM);
+  a.n_tiles = static_cast<int>((N + BN - 1) / BN);
+  a.k_blocks = static_cast<int>((K + C::kBK - 1) / C::kBK);
+  const int tiles = a.m_tiles * a.n_tiles;
+  const int grid = std::min(tiles, info.sm_count);
+  gemm_tf32x3_kernel<BN, BKB, SPLIT><<<grid, kThreads, C::kSmemBytes, stream>>>(mx, mhi, mlo, a);
+  return ko::check_launch("ko_linear_f32_packed");
+}
+
+using LaunchFn = int (*)(const float*, const float*, const float*, int64_t, int64_t, int64_t, int, float*, int*,
+                         cudaStream_t);
+
+struct Variant {
+  int bn, bkb, split;
+  LaunchFn fn;
+};
+
+const Variant kVariants[] = {
+    {256, 64, 1, launch_gemm<256, 64, true>},   {256, 64, 0, launch_gemm<256, 64, false>},
+    {192, 64, 1, launch_gemm<192, 64, true>},   {192, 64, 0, launch_gemm<192, 64, false>},
+    {128, 64, 1, launch_gemm<128, 64, true>},   {128, 64, 0, launch_gemm<128, 64, false>},
+    {256, 128, 1, launch_gemm<256, 128, true>}, {256, 128, 0, launch_gemm<256, 128, false>},
+    {128, 128, 1, launch_gemm<128, 128, true>}, {128, 128, 0, launch_gemm<128, 128, false>},
+};
+
+// Tuning override for measurements: KO_GEMM_VARIANT="bn,bkb,split" (e.g. "256,64,1").
+const Variant* forced_variant() {
+  static const Variant* v = [] {
+    const char* env = getenv("KO_GEMM_VARIANT");
+    if (!env) return static_cast<const Variant*>(nullptr);
+    int bn = 0, bkb = 0, split = 0;
+    if (sscanf(env, "%d,%d,%d", &bn, &bkb, &split) != 3) return static_cast<const Variant*>(nullptr);
+    for (const Variant& c : kVariants)
+      if (c.bn == bn && c.bkb == bkb && c.split == split) return &c;
+    return static_cast<const Variant*>(nullptr);
+  }();
+  return v;
+}
+
+// Default: 128-wide tiles with the split correction accumulator (two TMEM accumulator buffers fit, so the
+// epilogue of one tile overlaps the MMAs of the next), unless 192-wide tiles finish in one wave where
+// 128-wide tiles need two (small M).
+const Variant* choose_variant(int64_t M, int64_t N) {
+  if (const Variant* f = forced_variant()) return f;
+  const int64_t sms = ko::device_info().sm_count;
+  const int64_t m_tiles = (M + BM - 1) / BM;
+  const int64_t w128 = (m_tiles * ((N + 127) / 128) + sms - 1) / sms;
+  const int64_t w192 = (m_tiles * ((N + 191) / 192) + sms - 1) / sms;
+  const int bn = (w192 == 1 && w128 > 1) ? 192 : 128;
+  for (const Variant& c : kVariants)
+    if (c.bn == bn && c.bkb == 64 && c.split == 1) return &c;
+  return &kVariants[0];
+}
+
+int validate_linear(const float* x, const float* w, const float* bias, int64_t M, int64_t K, int64_t N,
+                    const float* out, const char* who) {
+  if (M < 0 || K < 4 || N < 4 || K % 4 != 0 || N % 4 != 0 || M > INT32_MAX || K > (1 << 20) || N > (1 << 20))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": need K % 4 == 0 and N % 4 == 0");
+  if (M == 0) return KO_OK;
+  if (!x || !w || !out) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": null pointer");
+  if (!ko::aligned16(x) || !ko::aligned16(w) || !ko::aligned16(out) || (bias && !ko::aligned16(bias)))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": pointers must be 16-byte aligned");
+  return KO_OK;
+}
+
+}  // namespace
+
+extern "C" int64_t ko_linear_workspace_bytes(int64_t K, int64_t N) { return 2 * K * N * 4; }
+
+extern "C" int ko_pack_weight_tf32x3(const float* w, int64_t K, int64_t N, float* w_packed, ko_stream_t stream) {
+  if (K < 1 || N < 1 || K > (1 << 20) || N > (1 << 20) || !w || !w_packed)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_pack_weight_tf32x3: bad arguments");
+  dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32));
+  pack_weight_kernel<<<grid, dim3(32, 8), 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      w, static_cast<int>(K), static_cast<int>(N), w_packed);
+  return ko::check_launch("ko_pack_weight_tf32x3");
+}
+
+extern "C" int ko_linear_f32_packed(const float* x, const float* w_packed, const float* bias, int64_t M, int64_t K,
+                                    int64_t N, int act, float* out, int* dev_status, ko_stream_t stream) {
+  int st = validate_linear(x, w_packed, bias, M, K, N, out, "ko_linear_f32_packed");
+  if (st || M == 0) return st;
+  if (act != KO_ACT_NONE && act != KO_ACT_GELU && act != KO_ACT_RELU)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_linear_f32_packed: unknown activation");
+  const Variant* v = choose_variant(M, N);
+  return v->fn(x, w_packed, bias, M, K, N, act, out, dev_status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ko_linear_gelu_f32(const float* x, const float* w, const float* bias, int64_t M, int64_t K,
+                                  int64_t N, float* out, void* workspace, int64_t workspace_bytes, int* dev_status,
+                                  ko_stream_t stream) {
+  int st = validate_linear(x, w, bias, M, K, N, out, "ko_linear_gelu_f32");
+  if (st || M == 0) return st;
+  if (!workspace || !ko::aligned16(workspace) || workspace_bytes < ko_linear_workspace_bytes(K, N))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_linear_gelu_f32: workspace missing, unaligned or too small");
+  float* packed = static_cast<float*>(workspace);
+  st = ko_pack_weight_tf32x3(w, K, N, packed, stream);
+  if (st) return st;
+  return ko_linear_f32_packed(x, packed, bias, M, K, N, KO_ACT_GELU, out, dev_status, stream);
+}

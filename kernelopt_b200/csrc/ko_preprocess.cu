@@ -1,0 +1,188 @@
+// uint8 BGR frame -> resized (cv2 INTER_LINEAR, bit-exact through the 4-tap tables), RGB, normalised float32.
+//
+// Semantics follow the reference kernel fast_rfdetr/kernels.py:74-103 (bgr_resize_normalize): for output row y
+// and BGR element e = x*3 + c the taps are A = top[xt.x], B = top[xt.y], C = bot[xt.x], D = bot[xt.y] with
+// xt = xtab[e], (top, bot) = rows ytab[y].x / ytab[y].y; the tap arithmetic is mode 0 (KleidiCV) or mode 1
+// (OpenCV); v is clamped to 0..255 and the RGB output channel 2-c receives lut[(2-c)*256 + v].
+//
+// B200 design: one CTA per (output row, image). The CTA stages the two source rows it needs in shared memory
+// with 16-byte loads, then every thread produces 4 consecutive outputs and writes them with one 128-bit store,
+// so both the row reads and the output writes are fully coalesced. All images of a batch (any sizes) go in one
+// launch. Three output layouts share the kernel: HWC (the reference's), CHW (NCHW batches) and PATCH16 (the
+// im2col of the ViT 16x16 patch embedding, which turns that convolution into a plain GEMM).
+#include <cstring>
+
+#include "ko_common.cuh"
+
+namespace {
+
+constexpr int kMaxImages = 64;
+constexpr int kThreads = 128;
+
+struct ImageParams {
+  const uint8_t* src;
+  const int4* xtab;
+  const int4* ytab;
+  int64_t src_h, src_w, src_stride;
+  int32_t mode;
+  int32_t vec_ok;  // rows start 16-byte aligned and src_w*3 is a multiple of 16
+};
+
+struct BatchParams {
+  ImageParams img[kMaxImages];
+};
+
+__device__ __forceinline__ int tap_value(int mode, const uint8_t* top, const uint8_t* bot, int4 xt, int4 yt,
+                                         int last) {
+  const int l = min(max(xt.x, 0), last), r = min(max(xt.y, 0), last);
+  const int A = top[l], B = top[r], C = bot[l], D = bot[r];
+  int v;
+  if (mode == 0) {
+    const int left = (A * 256 + (C - A) * yt.z + 128) >> 8;
+    const int right = (B * 256 + (D - B) * yt.z + 128) >> 8;
+    v = (left * 256 + (right - left) * xt.z + 128) >> 8;
+  } else {
+    const int h0 = A * xt.z + B * xt.w;
+    const int h1 = C * xt.z + D * xt.w;
+    v = ((((h0 >> 4) * yt.z) >> 16) + (((h1 >> 4) * yt.w) >> 16) + 2) >> 2;
+  }
+  return min(max(v, 0), 255);
+}
+
+__global__ void __launch_bounds__(kThreads) preprocess_kernel(const __grid_constant__ BatchParams p,
+                                                              const float* __restrict__ lut, int dst, int layout,
+                                                              float* __restrict__ out, int row_cap) {
+  extern __shared__ __align__(16) uint8_t rows[];  // [2][row_cap]
+  const ImageParams& im = p.img[blockIdx.y];
+  const int y = blockIdx.x;
+  const int4 yt = __ldg(im.ytab + y);
+  const int rmax = static_cast<int>(im.src_h) - 1;
+  const int r0 = min(max(yt.x, 0), rmax), r1 = min(max(yt.y, 0), rmax);
+  const int row_bytes = static_cast<int>(im.src_w) * 3;
+  const uint8_t* g0 = im.src + static_cast<int64_t>(r0) * im.src_stride;
+  const uint8_t* g1 = im.src + static_cast<int64_t>(r1) * im.src_stride;
+  uint8_t* s0 = rows;
+  uint8_t* s1 = rows + row_cap;
+
+  if (im.vec_ok) {
+    const int n16 = row_bytes >> 4;
+    const uint4* a = reinterpret_cast<const uint4*>(g0);
+    const uint4* b = reinterpret_cast<const uint4*>(g1);
+    for (int i = threadIdx.x; i < n16; i += kThreads) {
+      const uint4 va = __ldg(a + i), vb = __ldg(b + i);
+      reinterpret_cast<uint4*>(s0)[i] = va;
+      reinterpret_cast<uint4*>(s1)[i] = vb;
+    }
+  } else {
+    for (int i = threadIdx.x; i < row_bytes; i += kThreads) {
+      s0[i] = __ldg(g0 + i);
+      s1[i] = __ldg(g1 + i);
+    }
+  }
+  __syncthreads();
+
+  const int n_items = dst * 3 / 4;  // float4 outputs per row
+  const int per_ch = dst / 4;
+  const int last = row_bytes - 1;
+  const int64_t img_base = static_cast<int64_t>(blockIdx.y) * dst * dst * 3;
+  for (int i = threadIdx.x; i < n_items; i += kThreads) {
+    float v[4];
+    int64_t addr;
+    if (layout == KO_LAYOUT_CHW) {
+      const int c_rgb = i / per_ch, x0 = (i - c_rgb * per_ch) * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int e = (x0 + j) * 3 + (2 - c_rgb);
+        const int t = tap_value(im.mode, s0, s1, __ldg(im.xtab + e), yt, last);
+        v[j] = __ldg(lut + c_rgb * 256 + t);
+      }
+      addr = img_base + static_cast<int64_t>(c_rgb) * dst * dst + static_cast<int64_t>(y) * dst + x0;
+    } else {
+      const int o0 = i * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int o = o0 + j, x = o / 3, c_rgb = o - x * 3;
+        const int e = x * 3 + (2 - c_rgb);
+        const int t = tap_value(im.mode, s0, s1, __ldg(im.xtab + e), yt, last);
+        v[j] = __ldg(lut + c_rgb * 256 + t);
+      }
+      if (layout == KO_LAYOUT_HWC) {
+        addr = img_base + static_cast<int64_t>(y) * dst * 3 + o0;
+      } else {  // PATCH16: token (y/16, px) holds 16 rows of 48 floats
+        const int px = o0 / 48, within = o0 - px * 48;
+        const int token = (y >> 4) * (dst >> 4) + px;
+        addr = img_base + static_cast<int64_t>(token) * 768 + (y & 15) * 48 + within;
+      }
+    }
+    *reinterpret_cast<float4*>(out + addr) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+int validate_image(const ko_image_desc& d, int64_t dst, const char* who) {
+  if (!d.src || !d.xtab || !d.ytab) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": null pointer");
+  if (d.src_h < 1 || d.src_w < 1 || d.src_stride < d.src_w * 3 || d.src_w > (1 << 20) || d.src_h > (1 << 20))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": bad image size or stride");
+  if (d.mode != 0 && d.mode != 1) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": mode must be 0 or 1");
+  if (!ko::aligned16(d.xtab) || !ko::aligned16(d.ytab))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": tables must be 16-byte aligned");
+  (void)dst;
+  return KO_OK;
+}
+
+}  // namespace
+
+extern "C" int ko_preprocess_batch(const ko_image_desc* images, int n, const float* lut, int64_t dst, int layout,
+                                   float* out, ko_stream_t stream) {
+  const char* who = "ko_preprocess";
+  if (n < 1 || n > kMaxImages || !images) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_preprocess: 1..64 images per call");
+  if (!lut || !out || !ko::aligned16(out)) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_preprocess: lut/out null or out unaligned");
+  if (layout != KO_LAYOUT_HWC && layout != KO_LAYOUT_CHW && layout != KO_LAYOUT_PATCH16)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_preprocess: unknown layout");
+  if (dst < 4 || dst > 8192 || dst % 4 != 0 || (layout == KO_LAYOUT_PATCH16 && dst % 16 != 0))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_preprocess: dst must be a multiple of 4 (16 for PATCH16)");
+  BatchParams p;
+  std::memset(&p, 0, sizeof p);
+  int64_t row_cap = 16;
+  for (int i = 0; i < n; ++i) {
+    const ko_image_desc& d = images[i];
+    int st = validate_image(d, dst, who);
+    if (st) return st;
+    ImageParams& q = p.img[i];
+    q.src = d.src;
+    q.xtab = reinterpret_cast<const int4*>(d.xtab);
+    q.ytab = reinterpret_cast<const int4*>(d.ytab);
+    q.src_h = d.src_h;
+    q.src_w = d.src_w;
+    q.src_stride = d.src_stride;
+    q.mode = d.mode;
+    q.vec_ok = ko::aligned16(d.src) && d.src_stride % 16 == 0 && (d.src_w * 3) % 16 == 0;
+    row_cap = std::max<int64_t>(row_cap, (d.src_w * 3 + 15) / 16 * 16);
+  }
+  const int64_t smem = 2 * row_cap;
+  const ko::DeviceInfo& info = ko::device_info();
+  if (smem > info.max_smem_optin) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_preprocess: source rows too wide");
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(preprocess_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return ko::fail(static_cast<int>(e), "ko_preprocess: cannot enable large shared memory");
+  }
+  dim3 grid(static_cast<unsigned>(dst), static_cast<unsigned>(n));
+  preprocess_kernel<<<grid, kThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      p, lut, static_cast<int>(dst), layout, out, static_cast<int>(row_cap));
+  return ko::check_launch("ko_preprocess");
+}
+
+extern "C" int ko_preprocess(const uint8_t* src, int64_t src_h, int64_t src_w, int64_t src_stride,
+                             const int32_t* xtab, const int32_t* ytab, const float* lut, int mode, int64_t dst,
+                             int layout, float* out, ko_stream_t stream) {
+  ko_image_desc d;
+  d.src = src;
+  d.xtab = xtab;
+  d.ytab = ytab;
+  d.src_h = src_h;
+  d.src_w = src_w;
+  d.src_stride = src_stride;
+  d.mode = mode;
+  d._pad = 0;
+  return ko_preprocess_batch(&d, 1, lut, dst, layout, out, stream);
+}

@@ -1,0 +1,220 @@
+"""The four hot-path kernels, with the reference's call signatures (fast_rfdetr/kernels.py), on torch CUDA tensors.
+
+    residual_layernorm(h, o, bias, scale, gamma, beta, eps) -> (h_out, y)     kernels.py:53
+    preprocess_gpu(img_u8, xtab, ytab, lut, mode, dst=640) -> [dst,dst,3]      kernels.py:106
+    deform_attn(value, loc, aw, grid_hw, nh, hd, offset=0) -> [B,NQ,NH*HD]     kernels.py:165
+    linear_gelu_f32(x, w, bias) -> [..., N]                                    kernels.py:271
+
+Every call goes to libkernelopt.so (hand-written sm_100a CUDA) on the caller's current CUDA stream. Outputs
+are freshly allocated; inputs are read-only and must be contiguous float32 (uint8/int32 for preprocessing)
+CUDA tensors. There is no CPU path: CPU tensors raise ValueError, a missing library raises RuntimeError.
+Beyond the reference's API: batched preprocessing (`preprocess_batch`) and the pre-split weight form of the
+GEMM (`pack_weight` / `linear`), which the model uses for every dense layer.
+"""
+from __future__ import annotations
+
+import threading
+import weakref
+
+import torch
+
+from . import _lib
+from ._lib import call
+
+LAYOUTS = {"hwc": _lib.KO_LAYOUT_HWC, "chw": _lib.KO_LAYOUT_CHW, "patch16": _lib.KO_LAYOUT_PATCH16}
+ACTS = {None: _lib.KO_ACT_NONE, "none": _lib.KO_ACT_NONE, "gelu": _lib.KO_ACT_GELU, "relu": _lib.KO_ACT_RELU}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need(t: torch.Tensor, name: str, dtype=torch.float32):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (there is no CPU path)")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+# ---- device-side status word for kernels with bounded waits ----
+_status: dict[int, torch.Tensor] = {}
+_status_lock = threading.Lock()
+
+
+def _dev_index(device) -> int:
+    if device is None:
+        return torch.cuda.current_device()
+    if isinstance(device, int):
+        return device
+    d = torch.device(device)
+    return d.index if d.index is not None else torch.cuda.current_device()
+
+
+def status_word(device=None) -> torch.Tensor:
+    """The int32 device word that bounded-wait kernels write KO_ERR_DEVICE_TIMEOUT into."""
+    idx = _dev_index(device)
+    with _status_lock:
+        if idx not in _status:
+            _status[idx] = torch.zeros(1, dtype=torch.int32, device=f"cuda:{idx}")
+        return _status[idx]
+
+
+def check_device_status(device=None) -> None:
+    """Synchronising check of the status word; raises KernelError (and clears it) if a kernel timed out."""
+    w = status_word(device)
+    v = int(w.item())
+    if v != 0:
+        w.zero_()
+        raise _lib.KernelError("device kernel", v, "an on-chip wait ran out; the results of that launch are invalid")
+
+
+# ---- residual + LayerNorm ----
+def residual_layernorm(h, o, bias, scale, gamma, beta, eps):
+    """Returns (h + (o + bias) * scale, LayerNorm of that). h, o: [..., C] float32, C % 4 == 0.
+
+    bias / scale may be None (0 / 1). Same contract as the reference (kernels.py:53-67), fp32 only."""
+    _need(h, "h")
+    _need(o, "o")
+    if h.shape != o.shape:
+        raise ValueError("h and o must have the same shape")
+    c = h.shape[-1]
+    for name, t in (("bias", bias), ("scale", scale), ("gamma", gamma), ("beta", beta)):
+        if t is None and name in ("gamma", "beta"):
+            raise ValueError(f"{name} is required")
+        if t is not None and (_need(t, name).numel() != c):
+            raise ValueError(f"{name} must have {c} elements")
+    rows = h.numel() // c if c else 0
+    h_out = torch.empty_like(h)
+    y = torch.empty_like(h)
+    call("ko_residual_layernorm", h.data_ptr(), o.data_ptr(), _ptr(bias), _ptr(scale), gamma.data_ptr(),
+         beta.data_ptr(), float(eps), rows, c, h_out.data_ptr(), y.data_ptr(), _stream())
+    return h_out, y
+
+
+def residual_layernorm_into(h, o, bias, scale, gamma, beta, eps, h_out, y):
+    """In-place variant for preallocated buffers (h_out may be h). No shape checks beyond the C ABI's."""
+    c = h.shape[-1]
+    call("ko_residual_layernorm", h.data_ptr(), o.data_ptr(), _ptr(bias), _ptr(scale), gamma.data_ptr(),
+         beta.data_ptr(), float(eps), h.numel() // c, c, h_out.data_ptr(), y.data_ptr(), _stream())
+    return h_out, y
+
+
+# ---- preprocessing ----
+def preprocess_gpu(img_u8, xtab, ytab, lut, mode, dst=640, layout="hwc", out=None):
+    """img_u8: uint8 [H, W, 3] (row-contiguous) CUDA tensor. Returns float32 [dst, dst, 3] normalised RGB
+    (layout 'hwc', as the reference), or [3, dst, dst] ('chw') or [(dst/16)^2, 768] ('patch16')."""
+    return preprocess_batch([(img_u8, xtab, ytab, mode)], lut, dst, layout, out=out)[0]
+
+
+def preprocess_batch(items, lut, dst=640, layout="hwc", out=None):
+    """items: list of (img_u8 [H,W,3], xtab, ytab, mode) of any sizes; one launch per 64 images.
+
+    Returns float32 [N, ...] in `layout` (written into `out` when given)."""
+    if layout not in LAYOUTS:
+        raise ValueError(f"layout must be one of {sorted(LAYOUTS)}")
+    _need(lut, "lut")
+    n = len(items)
+    shape = {"hwc": (n, dst, dst, 3), "chw": (n, 3, dst, dst), "patch16": (n, (dst // 16) ** 2, 768)}[layout]
+    if out is None:
+        out = torch.empty(shape, dtype=torch.float32, device=lut.device)
+    elif tuple(out.shape) != shape or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous float32 tensor of shape {shape}")
+    for start in range(0, n, 64):
+        chunk = items[start:start + 64]
+        descs = (_lib.ImageDesc * len(chunk))()
+        for d, (img, xt, yt, mode) in zip(descs, chunk):
+            _need(img, "img_u8", torch.uint8)
+            _need(xt, "xtab", torch.int32)
+            _need(yt, "ytab", torch.int32)
+            if img.dim() != 3 or img.shape[2] != 3:
+                raise ValueError("expected a uint8 BGR image of shape (H, W, 3)")
+            if xt.numel() != dst * 3 * 4 or yt.numel() != dst * 4:
+                raise ValueError("tables do not match dst")
+            d.src, d.xtab, d.ytab = img.data_ptr(), xt.data_ptr(), yt.data_ptr()
+            d.src_h, d.src_w, d.src_stride = img.shape[0], img.shape[1], img.shape[1] * 3
+            d.mode = int(mode)
+        call("ko_preprocess_batch", descs, len(chunk), lut.data_ptr(), dst, LAYOUTS[layout],
+             out[start].data_ptr(), _stream())
+    return out
+
+
+# ---- deformable sampling ----
+def deform_attn(value, loc, aw, grid_hw, nh, hd, offset=0):
+    """value [B, H*W, ROW] with this layer's heads at columns [offset, offset + nh*hd); loc [B, NQ, NH, NP, 2]
+    normalised x, y; aw [B, NQ, NH, NP]. Returns [B, NQ, NH*HD] float32 (kernels.py:165-181)."""
+    _need(value, "value")
+    loc = _need(loc.contiguous() if loc.dtype == torch.float32 else loc.float().contiguous(), "loc")
+    aw = _need(aw.contiguous() if aw.dtype == torch.float32 else aw.float().contiguous(), "aw")
+    b, n_tok, row = value.shape
+    nq, npts = loc.shape[1], loc.shape[-2]
+    gh, gw = grid_hw
+    if n_tok != gh * gw or loc.numel() != b * nq * nh * npts * 2 or aw.numel() != b * nq * nh * npts:
+        raise ValueError("deform_attn: inconsistent shapes")
+    out = torch.empty((b, nq, nh * hd), dtype=torch.float32, device=value.device)
+    call("ko_deform_attn", value.data_ptr(), loc.data_ptr(), aw.data_ptr(), b, nq, nh, hd, npts, gh, gw, row,
+         offset, out.data_ptr(), _stream())
+    return out
+
+
+# ---- 3xTF32 GEMM ----
+class PackedWeight:
+    """A [K, N] weight split once into tf32 hi/lo halves, transposed ([2, N, K]) for the tcgen05 GEMM."""
+
+    __slots__ = ("packed", "k", "n", "bias", "__weakref__")
+
+    def __init__(self, w: torch.Tensor, bias: torch.Tensor | None = None):
+        _need(w, "w")
+        if w.dim() != 2:
+            raise ValueError("w must be [K, N]")
+        self.k, self.n = w.shape
+        self.packed = torch.empty((2, self.n, self.k), dtype=torch.float32, device=w.device)
+        call("ko_pack_weight_tf32x3", w.data_ptr(), self.k, self.n, self.packed.data_ptr(), _stream())
+        self.bias = None if bias is None else _need(bias, "bias")
+
+
+def pack_weight(w, bias=None) -> PackedWeight:
+    return PackedWeight(w, bias)
+
+
+def linear(x, pw: PackedWeight, act=None, out=None):
+    """act(x @ W + bias) for x [..., K] float32 with W pre-split (fp32-grade 3xTF32 tcgen05 GEMM)."""
+    _need(x, "x")
+    if x.shape[-1] != pw.k:
+        raise ValueError(f"x has {x.shape[-1]} features, the weight expects {pw.k}")
+    m = x.numel() // pw.k
+    if out is None:
+        out = torch.empty((*x.shape[:-1], pw.n), dtype=torch.float32, device=x.device)
+    call("ko_linear_f32_packed", x.data_ptr(), pw.packed.data_ptr(), _ptr(pw.bias), m, pw.k, pw.n, ACTS[act],
+         out.data_ptr(), status_word(x.device).data_ptr(), _stream())
+    return out
+
+
+_pack_cache: "weakref.WeakKeyDictionary[torch.Tensor, tuple[int, PackedWeight]]" = weakref.WeakKeyDictionary()
+_pack_lock = threading.Lock()
+
+
+def linear_gelu_f32(x, w, bias):
+    """GELU(x @ w + bias) for float32 x [..., K], w [K, N], bias [N] (kernels.py:271-285).
+
+    The split of w is cached per weight tensor (and redone if the tensor is modified in place)."""
+    _need(x, "x")
+    _need(w, "w")
+    _need(bias, "bias")
+    with _pack_lock:
+        hit = _pack_cache.get(w)
+        if hit is None or hit[0] != w._version:
+            hit = (w._version, PackedWeight(w))
+            _pack_cache[w] = hit
+    pw = hit[1]
+    m = x.numel() // pw.k
+    out = torch.empty((*x.shape[:-1], pw.n), dtype=torch.float32, device=x.device)
+    call("ko_linear_f32_packed", x.data_ptr(), pw.packed.data_ptr(), bias.data_ptr(), m, pw.k, pw.n,
+         _lib.KO_ACT_GELU, out.data_ptr(), status_word(x.device).data_ptr(), _stream())
+    return out

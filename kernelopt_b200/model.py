@@ -1,0 +1,285 @@
+"""RF-DETR-Medium forward pass on B200: the reference's graph (fast_rfdetr/model.py) in torch CUDA ops, with
+the hot path on libkernelopt's sm_100a kernels.
+
+Call sites of the reference's kernels (model.py:122, 125, 131, 226) use the same kernels here:
+  residual_layernorm   after the attention out-projection and after fc2 (24 calls per frame); the decoder's
+                       post-norms LN(tgt + x) use it too (12 calls per frame, no bias/scale)
+  linear_gelu_f32      backbone fc1 (the 3xTF32 tcgen05 GEMM with the GELU epilogue)
+  deform_attn          decoder cross-attention sampling, on the one fused [B,1600,1024] value projection
+Every other dense layer (QKV, out-proj, fc2, the patch embedding, the projector's 1x1 and im2col'd 3x3 convs,
+the decoder linears) runs on the same fp32-grade tcgen05 GEMM; only the layers whose output width is not a
+multiple of 4 (11 classes, 4 box coordinates) use torch's fp32 matmul. Attention (SDPA), LayerNorms outside
+the fused sites, SiLU, softmax and top-300 are torch ops in fp32 with TF32 disabled.
+
+The input is the patch layout the preprocessing kernel writes (PATCH16: [B, 1600, 768]), which makes the
+16x16/16 patch-embedding convolution one GEMM; NHWC [B, 640, 640, 3] (the reference's input) is accepted too.
+Everything is shape-static, so a whole forward is captured in one CUDA graph per batch size (detector.py).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import kernels as K
+from .weights import BB, CA_HEADS, CA_POINTS, DEC, LAYER, PROJ
+
+FULL_ATTN = (3, 6, 9)
+TAPS = (2, 5, 8, 11)
+GRID, WIN, C, HEADS = 40, 20, 384, 6
+D_MODEL, SA_HEADS, N_QUERIES = 256, 8, 300
+
+
+def configure_numerics() -> None:
+    """fp32 everywhere: no TF32 in torch matmul/cuDNN (single-pass TF32 reorders the top-300 ranking)."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    torch.set_float32_matmul_precision("highest")
+
+
+class Dense:
+    """A linear layer x @ W + b: tcgen05 3xTF32 GEMM when the output width allows it, else torch fp32."""
+
+    def __init__(self, w: torch.Tensor, b: torch.Tensor | None):
+        self.k, self.n = w.shape
+        self.native = self.n % 4 == 0 and self.k % 4 == 0
+        if self.native:
+            self.pw = K.pack_weight(w.contiguous(), None if b is None else b.contiguous())
+        else:
+            self.w, self.b = w.contiguous(), b
+
+    def __call__(self, x: torch.Tensor, act=None) -> torch.Tensor:
+        if self.native:
+            return K.linear(x.contiguous(), self.pw, act)
+        y = x @ self.w
+        if self.b is not None:
+            y = y + self.b
+        if act == "relu":
+            y = torch.relu(y)
+        elif act == "gelu":
+            y = F.gelu(y)
+        return y
+
+
+class RFDETR:
+    def __init__(self, weights: dict[str, np.ndarray], device: torch.device | str = "cuda"):
+        configure_numerics()
+        self.device = torch.device(device)
+        dev = self.device
+        self.eps = {k[5:]: float(np.asarray(v).reshape(())) for k, v in weights.items() if k.startswith("_eps.")}
+        p = {}
+        for k, v in weights.items():
+            if k.startswith("_eps."):
+                continue
+            if k.endswith("self_attn.out_proj.weight"):  # stored [out, in]
+                v = v.T
+            p[k] = torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32)).to(dev)
+        self.p = p
+        K.status_word(dev)  # allocate before any graph capture
+        self._prepare()
+
+    # ---- parameters -------------------------------------------------------------------------------------
+    def _ln(self, key):
+        return self.p[key + ".weight"], self.p[key + ".bias"], self.eps[key + ".weight"]
+
+    def _prepare(self):
+        p = self.p
+        pos = p[BB + "embeddings.position_embeddings"][0]
+        self.cls = (p[BB + "embeddings.cls_token"][0, 0] + pos[0]).reshape(1, 1, C)
+        self.pos = pos[1:].contiguous()                                                     # [1600, C]
+        pw = p[BB + "embeddings.patch_embeddings.projection.weight"]                         # [C, 16, 16, 3]
+        self.patch = Dense(pw.reshape(C, 768).t().contiguous(), p[BB + "embeddings.patch_embeddings.projection.bias"])
+        self.layers = []
+        for i in range(12):
+            pre = LAYER.format(i)
+            att = pre + "attention.attention."
+            wqkv = torch.cat([p[att + n + ".weight"] for n in ("query", "key", "value")], 1)
+            bqkv = torch.cat([p[att + n + ".bias"] for n in ("query", "key", "value")])
+            nxt = LAYER.format(i + 1) + "norm1" if i < 11 else BB + "layernorm"
+            self.layers.append(dict(
+                qkv=Dense(wqkv, bqkv),
+                out=Dense(p[pre + "attention.output.dense.weight"], None),
+                out_b=p[pre + "attention.output.dense.bias"], ls1=p[pre + "layer_scale1.lambda1"],
+                norm2=self._ln(pre + "norm2"),
+                fc1=K.pack_weight(p[pre + "mlp.fc1.weight"], p[pre + "mlp.fc1.bias"]),
+                fc2=Dense(p[pre + "mlp.fc2.weight"], None),
+                fc2_b=p[pre + "mlp.fc2.bias"], ls2=p[pre + "layer_scale2.lambda1"],
+                next_norm=self._ln(nxt)))
+        self.norm1_0 = self._ln(LAYER.format(0) + "norm1")
+        self.final_ln = self._ln(BB + "layernorm")
+
+        def conv(key):
+            w = p[key + ".conv.weight"]                                                      # [out, kh, kw, in]
+            k = w.shape[1]
+            return dict(dense=Dense(w.reshape(w.shape[0], -1).t().contiguous(), None), k=k, ln=self._ln(key + ".bn"))
+
+        self.cv1 = conv(PROJ + "0.cv1")
+        self.bottlenecks = [(conv(PROJ + f"0.m.{j}.cv1"), conv(PROJ + f"0.m.{j}.cv2")) for j in range(3)]
+        self.cv2 = conv(PROJ + "0.cv2")
+        self.proj_ln = self._ln(PROJ + "1")
+
+        d = lambda key: Dense(p[key + ".weight"], p.get(key + ".bias"))  # noqa: E731
+        self.enc_output = d("transformer.enc_output.0")
+        self.enc_norm = self._ln("transformer.enc_output_norm.0")
+        self.enc_class = d("transformer.enc_out_class_embed.0")
+        self.enc_bbox = [d(f"transformer.enc_out_bbox_embed.0.layers.{j}") for j in range(3)]
+        self.valid = p["proposal_valid"]
+        self.props = p["proposals"]
+        rp = p["refpoint_embed"]
+        self.rp_xy, self.rp_ewh = rp[:, :2].contiguous(), torch.exp(rp[:, 2:]).contiguous()
+        self.dim_t = p["dim_t"]
+        self.query_feat = p["query_feat"]
+        self.rph = [d(DEC + f"ref_point_head.layers.{j}") for j in range(2)]
+        vp = [DEC + f"layers.{i}.cross_attn.value_proj" for i in range(4)]
+        self.vproj = Dense(torch.cat([p[k + ".weight"] for k in vp], 1), torch.cat([p[k + ".bias"] for k in vp]))
+        self.dec = []
+        for i in range(4):
+            pre = DEC + f"layers.{i}."
+            sa = pre + "self_attn."
+            wqk = torch.cat([p[sa + "q.weight"], p[sa + "k.weight"]], 1)
+            bqk = torch.cat([p[sa + "q.bias"], p[sa + "k.bias"]])
+            ca = pre + "cross_attn."
+            woff = torch.cat([p[ca + "sampling_offsets.weight"], p[ca + "attention_weights.weight"]], 1)
+            boff = torch.cat([p[ca + "sampling_offsets.bias"], p[ca + "attention_weights.bias"]])
+            self.dec.append(dict(
+                qk=Dense(wqk, bqk), v=d(sa + "v"), out=d(sa + "out_proj"), norm1=self._ln(pre + "norm1"),
+                offaw=Dense(woff, boff), oproj=d(ca + "output_proj"), norm2=self._ln(pre + "norm2"),
+                l1=d(pre + "linear1"), l2=d(pre + "linear2"), norm3=self._ln(pre + "norm3")))
+        self.dec_norm = self._ln(DEC + "norm")
+        self.class_embed = d("class_embed")
+        self.bbox_embed = [d(f"bbox_embed.layers.{j}") for j in range(3)]
+
+    # ---- backbone -----------------------------------------------------------------------------------------
+    @staticmethod
+    def _ln_op(x, ln):
+        w, b, eps = ln
+        return F.layer_norm(x, (x.shape[-1],), w, b, eps)
+
+    def backbone(self, patches: torch.Tensor):
+        """patches [B, 1600, 768] -> four feature maps [B, 40, 40, C] (model.py:84-105, fused path)."""
+        b = patches.shape[0]
+        t = self.patch(patches.reshape(b * GRID * GRID, 768)).reshape(b, GRID * GRID, C) + self.pos
+        t = t.reshape(b, 2, WIN, 2, WIN, C).permute(0, 1, 3, 2, 4, 5).reshape(b * 4, WIN * WIN, C)
+        h = torch.cat([self.cls.expand(b * 4, 1, C), t], 1).contiguous()                      # [4B, 401, C]
+        y = self._ln_op(h, self.norm1_0)
+        feats = []
+        for i, lyr in enumerate(self.layers):
+            h, y = self._vit_layer(i, lyr, h, y, b)
+            if i in TAPS:
+                feats.append(y if i == 11 else self._ln_op(h, self.final_ln))
+        return [f[:, 1:].reshape(b, 2, 2, WIN, WIN, C).permute(0, 1, 3, 2, 4, 5).reshape(b, GRID, GRID, C)
+                for f in feats]
+
+    def _vit_layer(self, i, lyr, h, y, b):
+        """model.py:113-132: attention, residual+LN, fc1+GELU, fc2, residual+LN (next layer's norm1)."""
+        n, L, _ = h.shape
+        nb, Lb = (b, 4 * L) if i in FULL_ATTN else (n, L)                                      # global: merge windows
+        qkv = lyr["qkv"](y.reshape(nb * Lb, C)).reshape(nb, Lb, 3, HEADS, C // HEADS)
+        q, k, v = (qkv[:, :, j].transpose(1, 2) for j in range(3))                             # [nb, 6, Lb, 64]
+        o = F.scaled_dot_product_attention(q, k, v, scale=1 / math.sqrt(C // HEADS))
+        o = lyr["out"](o.transpose(1, 2).reshape(n * L, C)).reshape(n, L, C)
+        w2, b2, e2 = lyr["norm2"]
+        h, y = K.residual_layernorm(h, o, lyr["out_b"], lyr["ls1"], w2, b2, e2)
+        m = K.linear(y, lyr["fc1"], "gelu")
+        o = lyr["fc2"](m)
+        wn, bn, en = lyr["next_norm"]
+        return K.residual_layernorm(h, o, lyr["fc2_b"], lyr["ls2"], wn, bn, en)
+
+    # ---- projector ----------------------------------------------------------------------------------------
+    def _convx(self, x, cv):
+        """conv (as GEMM; 3x3 through im2col) + channel LayerNorm + SiLU (model.py:148-158)."""
+        b, hh, ww, cin = x.shape
+        if cv["k"] == 1:
+            cols = x.reshape(b * hh * ww, cin)
+        else:
+            xp = F.pad(x, (0, 0, 1, 1, 1, 1))
+            cols = torch.cat([xp[:, dy:dy + hh, dx:dx + ww] for dy in range(3) for dx in range(3)], -1)
+            cols = cols.reshape(b * hh * ww, 9 * cin)
+        y = cv["dense"](cols)
+        y = self._ln_op(y, cv["ln"])
+        return F.silu(y).reshape(b, hh, ww, -1)
+
+    def projector(self, feats):
+        y = self._convx(torch.cat(feats, -1), self.cv1)
+        parts = [y[..., :128], y[..., 128:]]
+        for cv_a, cv_b in self.bottlenecks:
+            parts.append(self._convx(self._convx(parts[-1].contiguous(), cv_a), cv_b))
+        y = self._convx(torch.cat(parts, -1), self.cv2)
+        return self._ln_op(y, self.proj_ln)
+
+    # ---- query selection ------------------------------------------------------------------------------------
+    def _mlp3(self, x, layers):
+        x = layers[0](x, "relu")
+        x = layers[1](x, "relu")
+        return layers[2](x)
+
+    def select_queries(self, memory):
+        """model.py:175-185: class score per proposal, box refinement, top-300 by score."""
+        om = memory * self.valid
+        om = self._ln_op(self.enc_output(om), self.enc_norm)
+        scores = self.enc_class(om).amax(-1)                                                    # [B, 1600]
+        delta = self._mlp3(om, self.enc_bbox)
+        prop = self.props
+        coord = torch.cat([delta[..., :2] * prop[:, 2:] + prop[:, :2], torch.exp(delta[..., 2:]) * prop[:, 2:]], -1)
+        idx = torch.topk(scores, N_QUERIES, dim=-1, largest=True, sorted=True).indices
+        ts = torch.gather(coord, 1, idx[..., None].expand(-1, -1, 4))
+        ref = torch.cat([self.rp_xy * ts[..., 2:] + ts[..., :2], self.rp_ewh * ts[..., 2:]], -1)
+        return ref, scores, idx
+
+    # ---- decoder ----------------------------------------------------------------------------------------------
+    def sine_embed(self, ref):
+        outs = []
+        for c in (1, 0, 2, 3):  # y, x, w, h
+            v = (ref[..., c] * (2 * math.pi))[..., None] / self.dim_t
+            outs.append(torch.stack([torch.sin(v[..., 0::2]), torch.cos(v[..., 1::2])], -1).reshape(*v.shape[:2], 128))
+        return torch.cat(outs, -1)
+
+    def _add_ln(self, x, r, ln):
+        w, b, eps = ln
+        return K.residual_layernorm(x.contiguous(), r.contiguous(), None, None, w, b, eps)[1]
+
+    def decoder(self, memory, ref):
+        b = memory.shape[0]
+        qpos = self.rph[1](self.rph[0](self.sine_embed(ref), "relu"))
+        tgt = self.query_feat.expand(b, N_QUERIES, D_MODEL).contiguous()
+        values = self.vproj(memory)                                                              # [B, 1600, 1024]
+        hd = D_MODEL // SA_HEADS
+        for i, lyr in enumerate(self.dec):
+            qk = lyr["qk"](tgt + qpos).reshape(b, N_QUERIES, 2, SA_HEADS, hd)
+            v = lyr["v"](tgt).reshape(b, N_QUERIES, SA_HEADS, hd).transpose(1, 2)
+            o = F.scaled_dot_product_attention(qk[:, :, 0].transpose(1, 2), qk[:, :, 1].transpose(1, 2), v,
+                                               scale=1 / math.sqrt(hd))
+            sa = lyr["out"](o.transpose(1, 2).reshape(b, N_QUERIES, D_MODEL))
+            tgt = self._add_ln(tgt, sa, lyr["norm1"])
+            oa = lyr["offaw"](tgt + qpos)                                                         # [B, 300, 96]
+            off = oa[..., :CA_HEADS * CA_POINTS * 2].reshape(b, N_QUERIES, CA_HEADS, CA_POINTS, 2)
+            aw = torch.softmax(oa[..., CA_HEADS * CA_POINTS * 2:].reshape(b, N_QUERIES, CA_HEADS, CA_POINTS), -1)
+            r = ref[:, :, None, None, :]
+            loc = r[..., :2] + off / CA_POINTS * r[..., 2:] * 0.5
+            s = K.deform_attn(values, loc, aw, (GRID, GRID), CA_HEADS, D_MODEL // CA_HEADS, offset=i * D_MODEL)
+            tgt = self._add_ln(tgt, lyr["oproj"](s), lyr["norm2"])
+            ffn = lyr["l2"](lyr["l1"](tgt, "relu"))
+            tgt = self._add_ln(tgt, ffn, lyr["norm3"])
+        return self._ln_op(tgt, self.dec_norm)
+
+    # ---- full forward -------------------------------------------------------------------------------------------
+    def forward(self, x: torch.Tensor):
+        """x: PATCH16 [B, 1600, 768] or NHWC [B, 640, 640, 3] normalised RGB.
+        Returns (boxes [B,300,4] cxcywh, logits [B,300,11]) float32 (model.py:261-272)."""
+        if x.dim() == 4:
+            b = x.shape[0]
+            x = x.reshape(b, GRID, 16, GRID, 16, 3).permute(0, 1, 3, 2, 4, 5).reshape(b, GRID * GRID, 768)
+        x = x.contiguous()
+        b = x.shape[0]
+        feats = self.backbone(x)
+        memory = self.projector(feats).reshape(b, GRID * GRID, D_MODEL)
+        ref, _, _ = self.select_queries(memory)
+        hs = self.decoder(memory, ref)
+        logits = self.class_embed(hs)
+        delta = self._mlp3(hs, self.bbox_embed)
+        boxes = torch.cat([delta[..., :2] * ref[..., 2:] + ref[..., :2], torch.exp(delta[..., 2:]) * ref[..., 2:]], -1)
+        return boxes, logits
+
+    __call__ = forward

@@ -1,0 +1,234 @@
+"""Parity of the four CUDA kernels with the CPU oracle, through the C ABI (libkernelopt.so via ctypes).
+
+Tolerances:
+  preprocessing  bit-exact (float32 bit patterns compared as uint32)
+  fp32 kernels   relative error <= 1e-5 in the max norm against the float64 oracle:
+                 max|gpu - ref| <= 1e-5 * max|ref| over the output tensor. (A per-element relative bound is
+                 meaningless where outputs cross zero; fp32 rounding of the sampling coordinates alone moves
+                 deform outputs by ~1e-6 of the map's scale, in the reference kernel as in this one.)
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle.kernels as OK
+import oracle.resize as OR
+from kernelopt_b200 import kernels as K
+from kernelopt_b200 import resize_tables as RT
+
+pytestmark = pytest.mark.gpu
+
+REL = 1e-5
+
+
+def assert_close(gpu, ref, rel=REL, what=""):
+    gpu = gpu.detach().cpu().double().numpy() if isinstance(gpu, torch.Tensor) else np.asarray(gpu, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert gpu.shape == ref.shape, (gpu.shape, ref.shape)
+    err = np.abs(gpu - ref)
+    scale = np.abs(ref).max()
+    assert np.isfinite(gpu).all(), f"{what}: non-finite output"
+    assert err.max() <= rel * scale, f"{what}: normwise error {err.max() / scale:.3e} > {rel}"
+
+
+def gpu_lut(dev):
+    return torch.from_numpy(OR.lut()).to(dev)
+
+
+def frame(h, w, seed, kind="noise"):
+    if kind == "noise":
+        return np.random.default_rng(seed).integers(0, 256, (h, w, 3), dtype=np.uint8)
+    y, x = np.mgrid[0:h, 0:w]
+    return np.stack([(x * 255 // max(w - 1, 1)), (y * 255 // max(h - 1, 1)), ((x + y) * 255 // max(h + w - 2, 1))],
+                    -1).astype(np.uint8)
+
+
+# ---------------------------------------------------------------- preprocessing
+@pytest.mark.parametrize("policy", ["reference", "opencv"])
+@pytest.mark.parametrize("hw", [(1080, 1920), (720, 1280), (540, 960), (1080, 1152), (500, 333), (641, 1279),
+                                (2160, 3840), (480, 640), (1000, 300)])
+def test_preprocess_bit_exact(cuda, policy, hw):
+    h, w = hw
+    lut = gpu_lut(cuda)
+    for kind in ("noise", "gradient"):
+        img = frame(h, w, h * w, kind)
+        mode, xt, yt = RT.tables(w, h, policy=policy)
+        g = K.preprocess_gpu(torch.from_numpy(img).to(cuda), torch.from_numpy(np.array(xt)).to(cuda),
+                             torch.from_numpy(np.array(yt)).to(cuda), lut, mode)
+        ref = OR.preprocess(img, policy=policy)
+        assert np.array_equal(g.cpu().numpy().view(np.uint32), ref.view(np.uint32)), (policy, hw, kind)
+
+
+def test_preprocess_matches_cv2_opencv_policy(cuda):
+    cv2 = pytest.importorskip("cv2")
+    lut = gpu_lut(cuda)
+    for h, w in [(1080, 1920), (720, 1280), (540, 960)]:
+        img = frame(h, w, 7 + h)
+        mode, xt, yt = RT.tables(w, h, policy="opencv")
+        g = K.preprocess_gpu(torch.from_numpy(img).to(cuda), torch.from_numpy(np.array(xt)).to(cuda),
+                             torch.from_numpy(np.array(yt)).to(cuda), lut, mode, layout="chw")
+        rgb = cv2.cvtColor(cv2.resize(img, (640, 640)), cv2.COLOR_BGR2RGB).astype(np.float32) / 255.
+        ref = np.ascontiguousarray(((rgb - OR.MEAN) / OR.STD).transpose(2, 0, 1))
+        assert np.array_equal(g.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("layout", ["hwc", "chw", "patch16"])
+def test_preprocess_batch_mixed_sizes(cuda, layout):
+    lut = gpu_lut(cuda)
+    sizes = [(1080, 1920), (720, 1280), (540, 960)]
+    imgs = [frame(h, w, 100 + i) for i, (h, w) in enumerate(sizes)]
+    items, refs = [], []
+    for img in imgs:
+        h, w, _ = img.shape
+        mode, xt, yt = RT.tables(w, h)
+        items.append((torch.from_numpy(img).to(cuda), torch.from_numpy(np.array(xt)).to(cuda),
+                      torch.from_numpy(np.array(yt)).to(cuda), mode))
+        refs.append(OR.preprocess(img, layout=layout))
+    out = K.preprocess_batch(items, lut, layout=layout)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), np.stack(refs).view(np.uint32))
+
+
+def test_preprocess_rejects_bad_input(cuda):
+    lut = gpu_lut(cuda)
+    mode, xt, yt = RT.tables(1920, 1080)
+    img = torch.zeros((1080, 1920, 3), dtype=torch.float32, device=cuda)
+    with pytest.raises(ValueError):
+        K.preprocess_gpu(img, torch.from_numpy(np.array(xt)).to(cuda), torch.from_numpy(np.array(yt)).to(cuda),
+                         lut, mode)
+    with pytest.raises(ValueError):
+        K.preprocess_gpu(img.to(torch.uint8), torch.from_numpy(np.array(xt)).to(cuda),
+                         torch.from_numpy(np.array(yt)).to(cuda), lut, mode, dst=320)
+
+
+# ---------------------------------------------------------------- residual + LayerNorm
+@pytest.mark.parametrize("batch", [1, 3, 64])
+def test_residual_layernorm(cuda, batch):
+    r = np.random.default_rng(batch)
+    rows, c = batch * 1600, 384
+    h = r.standard_normal((rows, c)).astype(np.float32)
+    o = r.standard_normal((rows, c)).astype(np.float32)
+    gamma = (1 + 0.1 * r.standard_normal(c)).astype(np.float32)
+    beta = (0.1 * r.standard_normal(c)).astype(np.float32)
+    bias = (0.1 * r.standard_normal(c)).astype(np.float32)
+    scale = (1 + 0.1 * r.standard_normal(c)).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    ho, y = K.residual_layernorm(t(h), t(o), t(bias), t(scale), t(gamma), t(beta), 1e-6)
+    rho, ry = OK.residual_layernorm(h, o, bias, scale, gamma, beta, 1e-6)
+    assert_close(ho, rho, what="h_out")
+    assert_close(y, ry, what="y")
+    ho, y = K.residual_layernorm(t(h), t(o), None, None, t(gamma), t(beta), 1e-6)
+    rho, ry = OK.residual_layernorm(h, o, None, None, gamma, beta, 1e-6)
+    assert_close(ho, rho, what="h_out (no bias/scale)")
+    assert_close(y, ry, what="y (no bias/scale)")
+
+
+@pytest.mark.parametrize("c", [256, 128, 4, 1024])
+def test_residual_layernorm_widths(cuda, c):
+    r = np.random.default_rng(c)
+    h = r.standard_normal((37, c)).astype(np.float32)
+    o = r.standard_normal((37, c)).astype(np.float32)
+    g = r.standard_normal(c).astype(np.float32)
+    b = r.standard_normal(c).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    ho, y = K.residual_layernorm(t(h), t(o), t(b), t(g), t(g), t(b), 1e-5)
+    rho, ry = OK.residual_layernorm(h, o, b, g, g, b, 1e-5)
+    assert_close(ho, rho)
+    assert_close(y, ry)
+
+
+# ---------------------------------------------------------------- deformable sampling
+def deform_inputs(r, b, row=256, nq=300, nh=16, npts=2):
+    value = r.standard_normal((b, 1600, row)).astype(np.float32)
+    loc = r.uniform(-0.05, 1.05, (b, nq, nh, 1, npts, 2)).astype(np.float32)
+    logits = r.standard_normal((b, nq, nh, npts))
+    aw = (np.exp(logits) / np.exp(logits).sum(-1, keepdims=True)).astype(np.float32)
+    return value, loc, aw
+
+
+@pytest.mark.parametrize("batch", [1, 3, 64])
+def test_deform_attn(cuda, batch):
+    r = np.random.default_rng(batch + 11)
+    value, loc, aw = deform_inputs(r, batch)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    g = K.deform_attn(t(value), t(loc).reshape(batch, 300, 16, 2, 2), t(aw), (40, 40), 16, 16)
+    ref = OK.deform_attn(value, loc.reshape(batch, 300, 16, 2, 2), aw, (40, 40), 16, 16)
+    assert_close(g, ref, what="deform")
+
+
+@pytest.mark.parametrize("offset", [0, 256, 512, 768])
+def test_deform_attn_fused_value_layout(cuda, offset):
+    r = np.random.default_rng(offset + 5)
+    value, loc, aw = deform_inputs(r, 2, row=1024)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    loc = loc.reshape(2, 300, 16, 2, 2)
+    g = K.deform_attn(t(value), t(loc), t(aw), (40, 40), 16, 16, offset=offset)
+    assert_close(g, OK.deform_attn(value, loc, aw, (40, 40), 16, 16, offset), what=f"offset {offset}")
+
+
+def test_deform_attn_scalar_path(cuda):
+    r = np.random.default_rng(3)
+    value = r.standard_normal((2, 12 * 7, 45)).astype(np.float32)
+    loc = r.uniform(-0.2, 1.2, (2, 9, 5, 3, 2)).astype(np.float32)
+    aw = r.uniform(0, 1, (2, 9, 5, 3)).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    g = K.deform_attn(t(value), t(loc), t(aw), (12, 7), 5, 7, offset=3)
+    assert_close(g, OK.deform_attn(value, loc, aw, (12, 7), 5, 7, 3), what="scalar path")
+
+
+# ---------------------------------------------------------------- 3xTF32 GEMM
+@pytest.mark.parametrize("m,k,n", [(1600, 384, 1536), (4800, 384, 1536), (51200, 384, 1536), (1604, 384, 1152),
+                                   (3208, 1536, 384), (6416, 384, 384), (1, 384, 1536), (130, 64, 256),
+                                   (1600, 256, 1024), (300, 100, 36), (1000, 768, 384)])
+def test_linear_gelu_3xtf32(cuda, m, k, n):
+    r = np.random.default_rng(m + k + n)
+    x = r.standard_normal((m, k)).astype(np.float32)
+    w = (0.02 * r.standard_normal((k, n))).astype(np.float32)
+    b = (0.01 * r.standard_normal(n)).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    g = K.linear_gelu_f32(t(x), t(w), t(b))
+    torch.cuda.synchronize()
+    K.check_device_status()
+    assert_close(g, OK.linear_gelu_f32(x, w, b), what=f"gemm {m}x{k}x{n}")
+
+
+@pytest.mark.parametrize("act", [None, "relu"])
+def test_linear_packed_acts(cuda, act):
+    r = np.random.default_rng(9)
+    x = r.standard_normal((777, 256)).astype(np.float32)
+    w = r.standard_normal((256, 512)).astype(np.float32)
+    b = r.standard_normal(512).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    pw = K.pack_weight(t(w), t(b))
+    g = K.linear(t(x), pw, act=act)
+    torch.cuda.synchronize()
+    K.check_device_status()
+    assert_close(g, OK.linear(x, w, b, act), what=str(act))
+
+
+def test_linear_gelu_workspace_entry_point(cuda):
+    """The C-ABI form that packs the weight into a caller-provided workspace on every call."""
+    from kernelopt_b200 import _lib
+    r = np.random.default_rng(21)
+    m, k, n = 3200, 384, 1536
+    x = torch.from_numpy(r.standard_normal((m, k)).astype(np.float32)).to(cuda)
+    w = torch.from_numpy((0.02 * r.standard_normal((k, n))).astype(np.float32)).to(cuda)
+    b = torch.from_numpy((0.01 * r.standard_normal(n)).astype(np.float32)).to(cuda)
+    ws = torch.empty(_lib.lib().ko_linear_workspace_bytes(k, n) // 4, dtype=torch.float32, device=cuda)
+    out = torch.empty((m, n), dtype=torch.float32, device=cuda)
+    _lib.call("ko_linear_gelu_f32", x.data_ptr(), w.data_ptr(), b.data_ptr(), m, k, n, out.data_ptr(),
+              ws.data_ptr(), ws.numel() * 4, K.status_word().data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    K.check_device_status()
+    assert_close(out, OK.linear_gelu_f32(x.cpu().numpy(), w.cpu().numpy(), b.cpu().numpy()))
+    with pytest.raises(ValueError):
+        _lib.call("ko_linear_gelu_f32", x.data_ptr(), w.data_ptr(), b.data_ptr(), m, k, n, out.data_ptr(),
+                  ws.data_ptr(), 16, None, torch.cuda.current_stream().cuda_stream)
+
+
+def test_linear_rejects_bad_shapes(cuda):
+    x = torch.zeros((10, 6), device=cuda)
+    w = torch.zeros((6, 8), device=cuda)
+    with pytest.raises(ValueError):
+        K.linear_gelu_f32(x, w, torch.zeros(8, device=cuda))

@@ -1,0 +1,76 @@
+"""Host-side wiring of the GPU model graph (kernelopt_b200.model) on the CPU: the kernel layer is replaced by
+float64 torch fakes (test doubles of the CUDA calls), so windowing, head splits, im2col ordering, the fused
+value projection and the decoder plumbing are checked against the oracle's unfused graph without a GPU."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle.kernels as OKn
+import oracle.resize as OR
+from kernelopt_b200.weights import random_weights
+from oracle.model import OracleRFDETR
+
+
+class _Packed:
+    def __init__(self, w, b=None):
+        self.w, self.b = w, b
+        self.k, self.n = w.shape
+
+
+def _linear(x, pw, act=None, out=None):
+    y = x @ pw.w
+    if pw.b is not None:
+        y = y + pw.b
+    if act == "gelu":
+        y = 0.5 * y * (1 + torch.erf(y / math.sqrt(2)))
+    elif act == "relu":
+        y = torch.relu(y)
+    return y
+
+
+def _rln(h, o, bias, scale, g, b, eps):
+    ho = h + (o + (0 if bias is None else bias)) * (1 if scale is None else scale)
+    return ho, F.layer_norm(ho, (ho.shape[-1],), g, b, eps)
+
+
+def _deform(value, loc, aw, grid_hw, nh, hd, offset=0):
+    return torch.from_numpy(OKn.deform_attn(value.numpy(), loc.numpy(), aw.numpy(), grid_hw, nh, hd, offset))
+
+
+@pytest.fixture()
+def cpu_model(monkeypatch):
+    import kernelopt_b200.kernels as K
+    import kernelopt_b200.model as M
+    monkeypatch.setattr(K, "pack_weight", lambda w, b=None: _Packed(w, b))
+    monkeypatch.setattr(K, "linear", _linear)
+    monkeypatch.setattr(K, "residual_layernorm", _rln)
+    monkeypatch.setattr(K, "deform_attn", _deform)
+    monkeypatch.setattr(K, "status_word", lambda *a: None)
+    w = random_weights(0)
+
+    class CPUModel(M.RFDETR):
+        def __init__(self, weights):
+            self.device = torch.device("cpu")
+            self.eps = {k[5:]: float(np.asarray(v).reshape(())) for k, v in weights.items() if k.startswith("_eps.")}
+            self.p = {k: torch.from_numpy(np.ascontiguousarray(v.T if k.endswith("self_attn.out_proj.weight") else v))
+                      .double() for k, v in weights.items() if not k.startswith("_eps.")}
+            self._prepare()
+
+    return CPUModel(w), OracleRFDETR(w, torch.float64)
+
+
+def test_model_graph_matches_oracle(cpu_model):
+    model, orc = cpu_model
+    img = np.random.default_rng(1).integers(0, 256, (720, 1280, 3), dtype=np.uint8)
+    x = torch.from_numpy(OR.preprocess(img))[None].double()
+    patches = torch.from_numpy(OR.preprocess(img, layout="patch16"))[None].double()
+    b1, l1 = model(patches)
+    b2, l2 = orc(x)
+    assert (b1 - b2).abs().max() < 1e-9 and (l1 - l2).abs().max() < 1e-9
+    b3, l3 = model(x)                     # NHWC input is accepted too
+    assert (b3 - b2).abs().max() < 1e-9 and (l3 - l2).abs().max() < 1e-9

@@ -1,0 +1,104 @@
+"""Runs one hot-path kernel at the benchmark configurations and reports its CUDA-event time and roofline.
+
+    python -m kernelopt_b200.profile_kernels --kernel gemm --batch 32 [--iters 20] [--warmup 3]
+
+Kernels and workloads (per frame of batch B; the algorithmic traffic or flops counted for the roofline):
+  preprocess  B frames, sizes cycling 1920x1080 / 1280x720 / 960x540 (B=1: 1080p only), seeded noise,
+              PATCH16 output; bytes = H*W*3 read + 640*640*3*4 written per frame
+  resln       rows = B*1600, C = 384, x/residual ~ N(0,1); bytes = 4 * rows * 384 * 4
+  gemm        GELU(A @ W + b), A [B*1600, 384] ~ N(0,1), W [384, 1536] ~ N(0, 0.02^2); flops = 2*M*384*1536
+  deform      value [B,1600,16,16], loc U[-0.05,1.05], softmax aw; bytes = 2,060,800 per frame
+Each timed iteration is bracketed by a write of a 256 MB buffer (larger than the 126 MB L2), outside the
+events, so every launch starts with a cold L2. One JSON line per run. Under ncu, use --iters 1-3.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+import torch
+
+from . import kernels as K
+from .benchutil import measured_peaks
+from .resize_tables import tables
+
+SIZES = [(1080, 1920), (720, 1280), (540, 960)]
+
+
+def setup(kernel: str, b: int, dev):
+    g = torch.Generator(device="cpu").manual_seed(0)
+    if kernel == "preprocess":
+        rng = np.random.default_rng(0)
+        sizes = [SIZES[0]] if b == 1 else [SIZES[i % 3] for i in range(b)]
+        lut = (np.arange(256, dtype=np.float32)[:, None] / 255. - np.asarray([.485, .456, .406], np.float32)) \
+            / np.asarray([.229, .224, .225], np.float32)
+        lut_d = torch.from_numpy(np.ascontiguousarray(lut.T)).to(dev)
+        items = []
+        for h, w in sizes:
+            mode, xt, yt = tables(w, h)
+            img = torch.from_numpy(rng.integers(0, 256, (h, w, 3), dtype=np.uint8)).to(dev)
+            items.append((img, torch.from_numpy(np.array(xt)).to(dev), torch.from_numpy(np.array(yt)).to(dev), mode))
+        out = torch.empty((b, 1600, 768), device=dev)
+        work = float(sum(h * w * 3 for h, w in sizes) + b * 640 * 640 * 3 * 4)
+        return (lambda: K.preprocess_batch(items, lut_d, 640, "patch16", out=out)), work, "byte"
+    if kernel == "resln":
+        rows = b * 1600
+        h = torch.randn(rows, 384, generator=g).to(dev)
+        o = torch.randn(rows, 384, generator=g).to(dev)
+        gamma = (1 + 0.1 * torch.randn(384, generator=g)).to(dev)
+        beta = (0.1 * torch.randn(384, generator=g)).to(dev)
+        return (lambda: K.residual_layernorm(h, o, None, None, gamma, beta, 1e-6)), 16.0 * rows * 384, "byte"
+    if kernel == "gemm":
+        m = b * 1600
+        a = torch.randn(m, 384, generator=g).to(dev)
+        w = (0.02 * torch.randn(384, 1536, generator=g)).to(dev)
+        bias = (0.01 * torch.randn(1536, generator=g)).to(dev)
+        pw = K.pack_weight(w, bias)
+        return (lambda: K.linear(a, pw, "gelu")), 2.0 * m * 384 * 1536, "flop"
+    if kernel == "deform":
+        value = torch.randn(b, 1600, 256, generator=g).to(dev)
+        loc = (torch.rand(b, 300, 16, 2, 2, generator=g) * 1.1 - 0.05).to(dev)
+        aw = torch.softmax(torch.randn(b, 300, 16, 2, generator=g), -1).to(dev)
+        return (lambda: K.deform_attn(value, loc, aw, (40, 40), 16, 16)), 2060800.0 * b, "byte"
+    raise ValueError(kernel)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", required=True, choices=["preprocess", "resln", "gemm", "deform"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args()
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device("cuda:0")
+    fn, work, unit = setup(args.kernel, args.batch, dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)   # 256 MB > L2
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.iters):
+        flush.fill_(1.0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / 1e3)
+    K.check_device_status(dev)
+    t = float(np.median(times))
+    peaks = measured_peaks()
+    if unit == "flop":
+        ach, peak, u = work / t / 1e12, peaks["bf16_tflops"] / 6.0, "TFLOP/s"
+    else:
+        ach, peak, u = work / t / 1e9, peaks["hbm_gbs"], "GB/s"
+    print(json.dumps({"kernel": args.kernel, "batch": args.batch, "median_us": t * 1e6, "min_us": min(times) * 1e6,
+                      "achieved": ach, "unit": u, "peak": peak, "frac": ach / peak,
+                      "peak_source": peaks["source"] + (" bf16/6 (3xTF32 ceiling)" if unit == "flop" else " HBM"),
+                      "work_per_launch": work, "iters": args.iters}), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -135,6 +135,20 @@ int ko_linear_f32_packed(const float* x, const float* w_packed, const float* bia
 int ko_linear_gelu_f32(const float* x, const float* w, const float* bias, int64_t M, int64_t K, int64_t N,
                        float* out, void* workspace, int64_t workspace_bytes, int* dev_status, ko_stream_t stream);
 
+/* out = GELU_erf(x @ w + bias) like ko_linear_gelu_f32, but needing no workspace: for callers that cannot
+ * allocate device memory at run time — applications whose allocator owns all GPU memory and forbids libraries
+ * to allocate, real-time per-frame paths where cudaMalloc/cudaFree can synchronise the device, plugin hosts that
+ * pass only input and output buffers. The weight split (2*K*N floats) goes to an 8 MiB array in the library's
+ * static device memory, held by every GPU that loads the library until exit; nothing is allocated per call.
+ * Limits: K*N <= KO_NOALLOC_MAX_WEIGHT_ELEMS, else KO_ERR_INVALID_ARGUMENT. All calls on a device share the
+ * array: calls that overlap on the GPU race and must be ordered (one stream, or events). Each call rewrites the
+ * part it reads first, so nothing needs clearing. The first call on a device looks up the array's address; make
+ * it before any stream capture on that device. No counterpart in the reference (its kernels run inside MLX,
+ * which allocates every buffer itself). */
+#define KO_NOALLOC_MAX_WEIGHT_ELEMS 1048576
+int ko_linear_gelu_f32_noalloc(const float* x, const float* w, const float* bias, int64_t M, int64_t K, int64_t N,
+                               float* out, int* dev_status, ko_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

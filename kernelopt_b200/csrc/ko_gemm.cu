@@ -475,3 +475,74 @@ extern "C" int ko_linear_gelu_f32(const float* x, const float* w, const float* b
   if (st) return st;
   return ko_linear_f32_packed(x, packed, bias, M, K, N, KO_ACT_GELU, out, dev_status, stream);
 }
+
+// ---------------------------------------------------------------------------------------------------------
+// ko_linear_gelu_f32_noalloc: ko_linear_gelu_f32 with its scratch in library-owned static device memory.
+//
+// For callers that cannot allocate device memory themselves at run time (they cannot provide the workspace
+// ko_linear_gelu_f32 asks for): applications whose allocator reserves all GPU memory up front and forbids
+// libraries to allocate behind its back, per-frame real-time paths where cudaMalloc/cudaFree may synchronise
+// the whole device and stall other streams, and plugin hosts that hand a plugin only its input and output
+// buffers. The scratch — the tf32 hi/lo split of the weight, 2*K*N floats — lives in the file-scope array
+// below instead, so this entry point never calls cudaMalloc, cudaFree or any allocating routine.
+//
+// Limits and sharing rules:
+//   * K*N <= KO_NOALLOC_MAX_WEIGHT_ELEMS (2^20 elements; the array is 8 MiB and every GPU that loads this
+//     library holds it until the process exits). Larger weights are rejected with KO_ERR_INVALID_ARGUMENT.
+//   * Every call shares the one array per device. Calls that overlap on the GPU (different streams, or other
+//     threads, without ordering between them) race on it and may produce wrong results: order them on one
+//     stream or with events.
+//   * Each call first rewrites the 2*K*N floats it uses, and the GEMM's tensor maps never read past them, so no
+//     contents need clearing between calls (what the previous call left is overwritten before it is read).
+//   * The first call on each device looks up the array's device address (cudaGetSymbolAddress, once per device,
+//     with that device current); make that first call before any stream capture on that device.
+// ---------------------------------------------------------------------------------------------------------
+#include <mutex>
+#include <vector>
+
+namespace {
+
+static __device__ __align__(256) float g_noalloc_wsplit[2 * KO_NOALLOC_MAX_WEIGHT_ELEMS];
+
+// Device address of g_noalloc_wsplit on the current device (looked up once per device). The symbol's name in
+// host code is only a host-side handle, never a device address, so it is never passed to a kernel itself.
+int noalloc_scratch(float** out) {
+  static std::mutex mu;
+  static std::vector<float*> addr;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return ko::fail(static_cast<int>(e), "ko_linear_gelu_f32_noalloc: cudaGetDevice failed");
+  std::lock_guard<std::mutex> lock(mu);
+  if (static_cast<int>(addr.size()) <= dev) addr.resize(dev + 1, nullptr);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_wsplit);
+    if (e != cudaSuccess || p == nullptr)
+      return ko::fail(static_cast<int>(e ? e : cudaErrorInvalidSymbol),
+                      std::string("ko_linear_gelu_f32_noalloc: cudaGetSymbolAddress failed: ") +
+                          cudaGetErrorString(e));
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return KO_OK;
+}
+
+}  // namespace
+
+extern "C" int ko_linear_gelu_f32_noalloc(const float* x, const float* w, const float* bias, int64_t M, int64_t K,
+                                          int64_t N, float* out, int* dev_status, ko_stream_t stream) {
+  int st = validate_linear(x, w, bias, M, K, N, out, "ko_linear_gelu_f32_noalloc");
+  if (st || M == 0) return st;
+  if (K * N > KO_NOALLOC_MAX_WEIGHT_ELEMS)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT,
+                    "ko_linear_gelu_f32_noalloc: K*N = " + std::to_string(K * N) +
+                        " exceeds the static scratch of KO_NOALLOC_MAX_WEIGHT_ELEMS = " +
+                        std::to_string(static_cast<long long>(KO_NOALLOC_MAX_WEIGHT_ELEMS)) +
+                        " weight elements; use ko_linear_gelu_f32 with a workspace instead");
+  float* scratch = nullptr;
+  st = noalloc_scratch(&scratch);
+  if (st) return st;
+  st = ko_pack_weight_tf32x3(w, K, N, scratch, stream);
+  if (st) return st;
+  return ko_linear_f32_packed(x, scratch, bias, M, K, N, KO_ACT_GELU, out, dev_status, stream);
+}

@@ -12,11 +12,13 @@
 // (ko_pack_weight_tf32x3); the activation split happens on chip, inside the pipeline, from the fp32 tile that
 // TMA brought in, so x is read from HBM exactly once.
 //
-// Kernel structure (persistent, one CTA per SM, 320 threads, warp-specialised):
-//   warp 0      TMA producer: x tile [128 x 32] and W_hi/W_lo tiles [BN x 32] per k-block, 128-byte swizzle
-//   warp 1      allocates TMEM; one lane issues the tcgen05.mma (12 per k-block: 4 k-steps x 3 products)
-//   warps 2-5   split the x tile in shared memory: hi in place, lo into a second buffer (same layout)
-//   warps 6-9   epilogue: TMEM -> registers (tcgen05.ld), + bias, activation, 128-bit stores
+// Kernel structure (persistent, one CTA per SM, 576 threads, warp-specialised):
+//   warp 0      TMA producer: x tile [128 x BK] and W_hi/W_lo tiles [BN x BK] per k-block, swizzled
+//   warp 1      allocates TMEM; one lane issues the tcgen05.mma (3 products per 8-wide k-step)
+//   warps 2-9   split the x tile in shared memory: hi in place, lo into a second buffer (same layout); two
+//               groups of four warps take alternate k-blocks
+//   warps 10-17 epilogue: TMEM -> registers (tcgen05.ld), + bias, activation, a swizzled 32x32 tile in shared
+//               memory per warp, TMA store (two warps per TMEM lane quadrant)
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the MMAs of tile i+1.
 // Every wait on an mbarrier is bounded (2 s); on timeout the CTA stops, drains what it issued, frees TMEM and
 // reports KO_ERR_DEVICE_TIMEOUT through dev_status.
@@ -31,10 +33,12 @@ namespace {
 using namespace kodev;
 
 constexpr int BM = 128;
-constexpr int kThreads = 320;
-constexpr int kTransformWarp0 = 2;
-constexpr int kEpilogueWarp0 = 6;
-constexpr size_t kSmemBudget = 224 * 1024;  // stage buffers; barriers and alignment slack come on top
+constexpr int kTransformWarp0 = 2;   // warps 2-9: two groups of four split alternate k-blocks
+constexpr int kEpilogueWarp0 = 10;   // warps 10-17: two warps per TMEM lane quadrant
+constexpr int kThreads = 18 * 32;
+constexpr uint32_t kStoreTileBytes = 32 * 32 * 4;                   // one epilogue warp's 32x32 output tile
+constexpr uint32_t kStoreBytes = 8 * kStoreTileBytes;               // 32 KB of staging for the TMA stores
+constexpr size_t kSmemBudget = 224 * 1024 - kStoreBytes;  // stage buffers; staging, barriers, slack on top
 
 // BN: tile width (MMA N). BKB: bytes of K per k-block row (128 -> 128-byte swizzle, 64 -> 64-byte swizzle).
 // SPLIT: accumulate the small hi*lo + lo*hi terms in their own TMEM accumulator and add it to the hi*hi
@@ -55,7 +59,7 @@ struct Cfg {
   static constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
                                         : kTmemNeed <= 256 ? 256 : 512;
   static constexpr uint32_t kTxBytes = kATileBytes + 2 * kBTileBytes;
-  static constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + 256 /*barriers*/;
+  static constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + kStoreBytes + 256;
   static constexpr uint32_t kSbo = 8 * BKB;                 // bytes between 8-row groups
   static constexpr uint32_t kLayout = BKB == 128 ? 2u : 4u;  // descriptor layout: 128B / 64B swizzle
   static_assert(kStages >= 2, "stage does not fit");
@@ -87,14 +91,16 @@ __device__ __forceinline__ uint64_t desc_k(uint32_t addr) {
 template <int BN, int BKB, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_whi,
-                       const __grid_constant__ CUtensorMap map_wlo, const GemmArgs args) {
+                       const __grid_constant__ CUtensorMap map_wlo, const __grid_constant__ CUtensorMap map_out,
+                       const GemmArgs args) {
   using C = Cfg<BN, BKB, SPLIT>;
   constexpr int S = C::kStages;
   constexpr int NB = C::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // stage st: [x -> hi][lo][W_hi][W_lo]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
+  // stage st: [x -> hi][lo][W_hi][W_lo]; then 8 epilogue staging tiles; then barriers
+  uint8_t* store_smem = smem + S * C::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(store_smem + kStoreBytes);
   uint64_t* full = bars;               // TMA landed            (1 arrival + tx bytes)
   uint64_t* ready = bars + S;          // x split done          (4 arrivals)
   uint64_t* empty = bars + 2 * S;      // MMAs of stage done    (1 commit)
@@ -115,7 +121,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], 8);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -123,6 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&map_x);
     prefetch_tmap(&map_whi);
     prefetch_tmap(&map_wlo);
+    prefetch_tmap(&map_out);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -223,37 +230,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < kEpilogueWarp0) {
     // ---------------- x split: hi in place, lo alongside ----------------
-    const int t = threadIdx.x - kTransformWarp0 * 32;  // 0..127
+    // Group g (warps 2-5 or 6-9) takes the k-blocks whose running index has parity g, so two stages are
+    // split at once and each group has two MMA k-blocks of time per stage.
+    const int group = (warp - kTransformWarp0) >> 2;
+    const int t = (threadIdx.x - kTransformWarp0 * 32) & 127;  // 0..127 within the group
     int st = 0;
     uint32_t phase = 0;
+    uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      for (int kb = 0; kb < args.k_blocks; ++kb) {
-        if (!mbar_wait(&full[st], phase, abort_flag)) {
-          ok = false;
-          break;
-        }
-        float4* xa = reinterpret_cast<float4*>(smem + st * C::kStageBytes);
-        float4* xl = reinterpret_cast<float4*>(smem + st * C::kStageBytes + C::kATileBytes);
+      for (int kb = 0; kb < args.k_blocks; ++kb, ++it) {
+        if ((it & 1u) == static_cast<uint32_t>(group)) {
+          if (!mbar_wait(&full[st], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          float4* xa = reinterpret_cast<float4*>(smem + st * C::kStageBytes);
+          float4* xl = reinterpret_cast<float4*>(smem + st * C::kStageBytes + C::kATileBytes);
 #pragma unroll
-        for (int i = 0; i < static_cast<int>(C::kATileBytes / 16 / 128); ++i) {
-          const int idx = t + i * 128;
-          const float4 v = xa[idx];
-          float4 hi, lo;
-          hi.x = __uint_as_float(f32_to_tf32_rna(v.x));
-          hi.y = __uint_as_float(f32_to_tf32_rna(v.y));
-          hi.z = __uint_as_float(f32_to_tf32_rna(v.z));
-          hi.w = __uint_as_float(f32_to_tf32_rna(v.w));
-          lo.x = __uint_as_float(f32_to_tf32_rna(v.x - hi.x));
-          lo.y = __uint_as_float(f32_to_tf32_rna(v.y - hi.y));
-          lo.z = __uint_as_float(f32_to_tf32_rna(v.z - hi.z));
-          lo.w = __uint_as_float(f32_to_tf32_rna(v.w - hi.w));
-          xa[idx] = hi;
-          xl[idx] = lo;
+          for (int i = 0; i < static_cast<int>(C::kATileBytes / 16 / 128); ++i) {
+            const int idx = t + i * 128;
+            const float4 v = xa[idx];
+            float4 hi, lo;
+            hi.x = __uint_as_float(f32_to_tf32_rna(v.x));
+            hi.y = __uint_as_float(f32_to_tf32_rna(v.y));
+            hi.z = __uint_as_float(f32_to_tf32_rna(v.z));
+            hi.w = __uint_as_float(f32_to_tf32_rna(v.w));
+            lo.x = __uint_as_float(f32_to_tf32_rna(v.x - hi.x));
+            lo.y = __uint_as_float(f32_to_tf32_rna(v.y - hi.y));
+            lo.z = __uint_as_float(f32_to_tf32_rna(v.z - hi.z));
+            lo.w = __uint_as_float(f32_to_tf32_rna(v.w - hi.w));
+            xa[idx] = hi;
+            xl[idx] = lo;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ready[st]);
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ready[st]);
         if (++st == S) {
           st = 0;
           phase ^= 1u;
@@ -262,8 +275,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue ----------------
+    // Warp pair per TMEM lane quadrant; half h of the pair takes the 32-column chunks c with c % 2 == h. Each
+    // chunk: tcgen05.ld of the main (and correction) accumulator, + bias, activation, a 128-byte-swizzled 32x32
+    // tile in shared memory, and one TMA store (rows >= M and columns >= N are clipped by the tensor map).
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-    const int row_in_tile = quad * 32 + lane;
+    const int half = (warp - kEpilogueWarp0) >> 2;
+    uint8_t* stile = store_smem + (warp - kEpilogueWarp0) * kStoreTileBytes;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int as = local % NB;
@@ -271,45 +288,53 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&acc_full[as], acc_phase, abort_flag)) break;
       tc_fence_after();
       const int m0 = (tile / args.n_tiles) * BM, n0 = (tile % args.n_tiles) * BN;
-      const int row = m0 + row_in_tile;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + as * C::kAccCols;
-      float* orow = args.out + static_cast<int64_t>(row) * args.N;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half; c < BN / 32; c += 2) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(taddr + c * 32, r);
-        tmem_ld_wait_regs(r);
         if constexpr (SPLIT) {
           uint32_t q[32];
           tmem_ld_32x32b_x32(taddr + BN + c * 32, q);
+          tmem_ld_wait_regs(r);
           tmem_ld_wait_regs(q);
 #pragma unroll
           for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
+        } else {
+          tmem_ld_wait_regs(r);
         }
-        if (c == BN / 32 - 1) {
+        if (c + 2 >= BN / 32) {  // this warp's last chunk of the tile: release the accumulator
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[as]);
         }
         const int col0 = n0 + c * 32;
-        if (row < args.M) {
+        // the previous TMA store from this warp's tile must have finished reading it
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const int col = col0 + j;
-            if (col < args.N) {
-              float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-              if (args.bias) b = __ldg(reinterpret_cast<const float4*>(args.bias + col));
-              float4 o;
-              o.x = apply_act(__uint_as_float(r[j + 0]) + b.x, args.act);
-              o.y = apply_act(__uint_as_float(r[j + 1]) + b.y, args.act);
-              o.z = apply_act(__uint_as_float(r[j + 2]) + b.z, args.act);
-              o.w = apply_act(__uint_as_float(r[j + 3]) + b.w, args.act);
-              *reinterpret_cast<float4*>(orow + col) = o;
-            }
-          }
+        for (int j = 0; j < 8; ++j) {
+          const int col = col0 + 4 * j;
+          float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (args.bias && col < args.N) b = __ldg(reinterpret_cast<const float4*>(args.bias + col));
+          float4 o;
+          o.x = apply_act(__uint_as_float(r[4 * j + 0]) + b.x, args.act);
+          o.y = apply_act(__uint_as_float(r[4 * j + 1]) + b.y, args.act);
+          o.z = apply_act(__uint_as_float(r[4 * j + 2]) + b.z, args.act);
+          o.w = apply_act(__uint_as_float(r[4 * j + 3]) + b.w, args.act);
+          // row `lane` of the tile, 16-byte chunk j, 128-byte swizzle: chunk position j ^ (row % 8)
+          *reinterpret_cast<float4*>(stile + lane * 128 + ((j ^ (lane & 7)) << 4)) = o;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_out, stile, col0, m0 + quad * 32);
+          bulk_commit();
         }
       }
     }
+    if (lane == 0) bulk_wait<0>();  // all stores complete before the CTA exits
+    __syncwarp();
   }
 
   __syncthreads();
@@ -361,6 +386,9 @@ int launch_gemm(const float* x, const float* w_packed, const float* bias, int64_
   if (st) return st;
   st = ko::make_tmap_2d_f32(&mlo, w_packed + N * K, N, K, K, BN, C::kBK, sw, "ko_linear w_lo");
   if (st) return st;
+  CUtensorMap mout;
+  st = ko::make_tmap_2d_f32(&mout, out, M, N, N, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, "ko_linear out");
+  if (st) return st;
   const ko::DeviceInfo& info = ko::device_info();
   if (static_cast<int64_t>(C::kSmemBytes) > info.max_smem_optin)
     return ko::fail(KO_ERR_UNSUPPORTED, "ko_linear: not enough shared memory on this device");
@@ -380,7 +408,7 @@ int launch_gemm(const float* x, const float* w_packed, const float* bias, int64_
   a.k_blocks = static_cast<int>((K + C::kBK - 1) / C::kBK);
   const int tiles = a.m_tiles * a.n_tiles;
   const int grid = std::min(tiles, info.sm_count);
-  gemm_tf32x3_kernel<BN, BKB, SPLIT><<<grid, kThreads, C::kSmemBytes, stream>>>(mx, mhi, mlo, a);
+  gemm_tf32x3_kernel<BN, BKB, SPLIT><<<grid, kThreads, C::kSmemBytes, stream>>>(mx, mhi, mlo, mout, a);
   return ko::check_launch("ko_linear_f32_packed");
 }
 

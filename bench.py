@@ -113,7 +113,7 @@ def instrumented_step(det, runner_x, items, K):
     """One eager (uncaptured) step with every hot-path kernel call wrapped in CUDA events on its launching
     stream. Returns {kernel: (seconds, work, launches, unit)} and the number of libkernelopt launches."""
     from kernelopt_b200 import _lib
-    from kernelopt_b200.benchutil import EventTimer
+    from kernelopt_b200.benchutil import EventTimer, hold_stream
 
     timers = {n: EventTimer() for n in ("gemm_tf32x3", "residual_layernorm", "deform_attn", "preprocess")}
     orig = {n: getattr(K, n) for n in ("linear", "residual_layernorm", "deform_attn", "preprocess_batch")}
@@ -139,6 +139,7 @@ def instrumented_step(det, runner_x, items, K):
     before = sum(_lib.launch_count.values())
     try:
         with __import__("torch").cuda.stream(det.stream):
+            hold_stream(0.3)   # the host enqueues the whole eager step first: events time GPU work only
             K.preprocess_batch(items, det._lut, 640, "patch16", out=runner_x)
             det.model(runner_x)
         det.stream.synchronize()

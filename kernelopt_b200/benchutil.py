@@ -111,6 +111,15 @@ class EventTimer:
         return secs, sum(w for _, _, w in self.pairs), len(self.pairs)
 
 
+def hold_stream(seconds: float = 0.05, stream=None) -> None:
+    """Keeps `stream` busy for about `seconds` with a spin kernel, so that the host enqueues the launches that
+    follow before the GPU reaches them: CUDA events around each of those launches then time the GPU's work
+    alone, not the host's Python and launch overhead that would otherwise sit between the two events."""
+    s = stream or torch.cuda.current_stream()
+    with torch.cuda.stream(s):
+        torch.cuda._sleep(int(seconds * 2.0e9))  # cycles; B200 SM clocks run at about 2 GHz or below
+
+
 class Stopwatch:
     def __enter__(self):
         self.t0 = time.perf_counter()

@@ -6,12 +6,16 @@
 //   x = loc_x * GW - 0.5, y = loc_y * GH - 0.5, x0 = floor(x), fx = x - x0 (same for y); taps outside the
 //   GH x GW map contribute 0; s_p = sum over the 4 taps of w_x * w_y * value; out = sum_p aw_p * s_p.
 //
-// B200 design. The value map of one frame and layer is 40x40 tokens x 256 channels (1.6 MB) — too large for
-// shared memory, but the whole batch of maps stays resident in the 126 MB L2 while it is sampled. Four lanes
-// serve one (query, head): each lane owns 4 of the head's 16 channels, so a tap is one 64-byte contiguous read
-// by a lane quad (128-bit loads, 2 full sectors), the quad's sampling coordinates are broadcast loads, and the
-// output of a warp (8 heads x 64 bytes) is one contiguous 512-byte store. A scalar kernel covers head sizes or
-// column offsets that are not multiples of 4.
+// B200 design. The value map of one frame and layer is 40x40 tokens x 256 channels (1.6 MB); the batch's maps
+// stay resident in the 126 MB L2 while they are sampled, so the kernels gather straight from global memory.
+// Four lanes serve one (query, head): each lane owns 4 of the head's 16 channels, so a tap is one 64-byte
+// contiguous read by a lane quad (128-bit loads, 2 full sectors), the quad's sampling coordinates are broadcast
+// loads, and the output of a warp (8 heads x 64 bytes) is one contiguous 512-byte store. With the model's two
+// points per head, every thread issues all 8 of its tap loads before its first multiply (deform_vec4_np2_kernel),
+// which keeps enough loads in flight to cover the HBM latency of the gather. (Staging each head's 100 KB slice
+// of the map in shared memory, one CTA per (frame, head), measured slower on B200: 45 us against 31 us at
+// 64 frames — two such CTAs per SM alternate between copying and sampling instead of overlapping many gathers.)
+// A scalar kernel covers head sizes or column offsets that are not multiples of 4.
 #include "ko_common.cuh"
 
 namespace {
@@ -68,6 +72,58 @@ __global__ void __launch_bounds__(256) deform_vec4_kernel(const float* __restric
       }
     }
     fma4(acc, w, sacc);
+  }
+  reinterpret_cast<float4*>(out)[t] = acc;
+}
+
+// Two points per (query, head), the model's layout: each thread reads its (query, head)'s locations (16 bytes)
+// and weights (8 bytes) with one load each and then issues all 8 of its tap loads before the first multiply, so
+// a thread keeps its whole gather in flight at once instead of one point at a time.
+__global__ void __launch_bounds__(256) deform_vec4_np2_kernel(const float* __restrict__ value,
+                                                              const float* __restrict__ loc,
+                                                              const float* __restrict__ aw, DeformShape s,
+                                                              float* __restrict__ out) {
+  const int64_t groups = s.HD >> 2;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = s.B * s.NQ * s.NH * groups;
+  if (t >= total) return;
+  const int64_t g = t % groups;
+  const int64_t qh = t / groups;  // (b*NQ + q)*NH + h
+  const int64_t h = qh % s.NH;
+  const int64_t b = qh / (s.NH * s.NQ);
+  const int GW = static_cast<int>(s.GW), GH = static_cast<int>(s.GH);
+  const float* vb = value + b * (s.GH * s.GW * s.ROW) + s.offset + h * s.HD + g * 4;
+  const float4 l = __ldg(reinterpret_cast<const float4*>(loc) + qh);   // (x0, y0, x1, y1)
+  const float2 w = __ldg(reinterpret_cast<const float2*>(aw) + qh);
+  float4 v[8];
+  float wt[8];
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const float lx = (p ? l.z : l.x) * static_cast<float>(GW) - 0.5f;
+    const float ly = (p ? l.w : l.y) * static_cast<float>(GH) - 0.5f;
+    const float x0f = floorf(lx), y0f = floorf(ly);
+    const float fx = lx - x0f, fy = ly - y0f;
+    const int x0 = static_cast<int>(x0f), y0 = static_cast<int>(y0f);
+#pragma unroll
+    for (int dy = 0; dy < 2; ++dy) {
+#pragma unroll
+      for (int dx = 0; dx < 2; ++dx) {
+        const int k = p * 4 + dy * 2 + dx;
+        const int yy = y0 + dy, xx = x0 + dx;
+        const bool in = yy >= 0 && yy < GH && xx >= 0 && xx < GW;
+        wt[k] = in ? (dx ? fx : 1.0f - fx) * (dy ? fy : 1.0f - fy) : 0.0f;
+        v[k] = in ? __ldg(reinterpret_cast<const float4*>(vb + static_cast<int64_t>(yy * GW + xx) * s.ROW))
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  }
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    float4 sacc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) fma4(sacc, wt[p * 4 + k], v[p * 4 + k]);
+    fma4(acc, p ? w.y : w.x, sacc);
   }
   reinterpret_cast<float4*>(out)[t] = acc;
 }
@@ -129,7 +185,11 @@ extern "C" int ko_deform_attn(const float* value, const float* loc, const float*
   const int64_t total = B * NQ * NH * (vec ? HD / 4 : HD);
   const int64_t blocks = (total + 255) / 256;
   if (blocks > 0x7fffffff) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_deform_attn: problem too large");
-  if (vec)
+  const bool np2 = vec && NP == 2 && (reinterpret_cast<uintptr_t>(loc) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(aw) & 7) == 0;
+  if (np2)
+    deform_vec4_np2_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(value, loc, aw, s, out);
+  else if (vec)
     deform_vec4_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(value, loc, aw, s, out);
   else
     deform_scalar_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(value, loc, aw, s, out);

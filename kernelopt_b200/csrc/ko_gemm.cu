@@ -442,18 +442,36 @@ const Variant* forced_variant() {
   return v;
 }
 
-// Default: 128-wide tiles with the split correction accumulator (two TMEM accumulator buffers fit, so the
-// epilogue of one tile overlaps the MMAs of the next), unless 192-wide tiles finish in one wave where
-// 128-wide tiles need two (small M).
-const Variant* choose_variant(int64_t M, int64_t N) {
+// Default choice.
+//   Accumulator: the split correction accumulator (SPLIT) only for K > 512. Up to K = 512 the single accumulator
+//   stays within 3e-6 of float64 (normwise, N(0,1) activations, K = 384) — inside the 1e-5 bar with room — and
+//   leaves TMEM for two accumulator buffers at 256 columns, so the epilogue of one tile overlaps the MMAs of the
+//   next. Beyond that its error grows with K (1.1e-5 at K = 1536), and SPLIT keeps it at 4e-6.
+//   Tile width: the BN in {256, 192, 128} with the least estimated time, waves x BN x cost per column, where
+//   the cost per column (1, 1.12, 1.45 without SPLIT) was measured on B200 at the model's shapes: wider tiles read
+//   each x tile from shared memory for more columns. With SPLIT, 256-wide tiles hold all 512 TMEM columns (one
+//   buffer) and lose the overlap, so they cost more per column than 192-wide ones.
+const Variant* choose_variant(int64_t M, int64_t N, int64_t K) {
   if (const Variant* f = forced_variant()) return f;
+  const int split = K > 512 ? 1 : 0;
   const int64_t sms = ko::device_info().sm_count;
   const int64_t m_tiles = (M + BM - 1) / BM;
-  const int64_t w128 = (m_tiles * ((N + 127) / 128) + sms - 1) / sms;
-  const int64_t w192 = (m_tiles * ((N + 191) / 192) + sms - 1) / sms;
-  const int bn = (w192 == 1 && w128 > 1) ? 192 : 128;
+  const int bns[3] = {256, 192, 128};
+  const double cost_plain[3] = {1.0, 1.12, 1.45};
+  const double cost_split[3] = {1.12, 1.0, 1.45};
+  int best = 0;
+  double best_t = 0;
+  for (int i = 0; i < 3; ++i) {
+    const int64_t tiles = m_tiles * ((N + bns[i] - 1) / bns[i]);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const double t = static_cast<double>(waves) * bns[i] * (split ? cost_split[i] : cost_plain[i]);
+    if (i == 0 || t < best_t) {
+      best = i;
+      best_t = t;
+    }
+  }
   for (const Variant& c : kVariants)
-    if (c.bn == bn && c.bkb == 64 && c.split == 1) return &c;
+    if (c.bn == bns[best] && c.bkb == 64 && c.split == split) return &c;
   return &kVariants[0];
 }
 
@@ -487,7 +505,7 @@ extern "C" int ko_linear_f32_packed(const float* x, const float* w_packed, const
   if (st || M == 0) return st;
   if (act != KO_ACT_NONE && act != KO_ACT_GELU && act != KO_ACT_RELU)
     return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_linear_f32_packed: unknown activation");
-  const Variant* v = choose_variant(M, N);
+  const Variant* v = choose_variant(M, N, K);
   return v->fn(x, w_packed, bias, M, K, N, act, out, dev_status, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -5,9 +5,11 @@
 // xt = xtab[e], (top, bot) = rows ytab[y].x / ytab[y].y; the tap arithmetic is mode 0 (KleidiCV) or mode 1
 // (OpenCV); v is clamped to 0..255 and the RGB output channel 2-c receives lut[(2-c)*256 + v].
 //
-// B200 design: one CTA per (output row, image). The CTA stages the two source rows it needs in shared memory
-// with 16-byte loads, then every thread produces 4 consecutive outputs and writes them with one 128-bit store,
-// so both the row reads and the output writes are fully coalesced. All images of a batch (any sizes) go in one
+// B200 design: every thread produces 4 consecutive outputs and writes them with one 128-bit store, from source
+// rows staged in shared memory with 16-byte copies, so both the row reads and the output writes are fully
+// coalesced. Outputs up to 682 wide (the model's 640) use the band kernel: one CTA per band of output rows, with
+// the x taps in registers, the LUT in shared memory and the next row pair prefetched with cp.async while the
+// current one is computed. Wider outputs use one CTA per output row. All images of a batch (any sizes) go in one
 // launch. Three output layouts share the kernel: HWC (the reference's), CHW (NCHW batches) and PATCH16 (the
 // im2col of the ViT 16x16 patch embedding, which turns that convolution into a plain GEMM).
 #include <cstring>
@@ -118,6 +120,178 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(const __grid_const
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// Band kernel (dst * 3 / 4 <= 2 * kBandThreads float4 outputs per row, i.e. dst <= 682; the 640 of the model).
+//
+// One CTA per (band of `band` consecutive output rows, image); each thread owns one or two float4 slots of the
+// output row.
+// Everything that does not depend on the row is set up once per CTA and kept on chip: each thread's x taps (the
+// clamped xtab entries of its 4 output elements), their RGB channels and output column offset live in registers, the
+// 768-entry LUT in shared memory. The two source rows of output row y+1 are fetched with cp.async (16-byte,
+// L2-only) into the other half of a double buffer while row y is computed, so the HBM reads of the next row
+// overlap the arithmetic of this one. Per output element the loop does 4 byte loads from shared memory, the
+// integer tap arithmetic, one LUT load from shared memory and a quarter of a 128-bit store.
+// ---------------------------------------------------------------------------------------------------------
+constexpr int kBandThreads = 256;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(kodev::smem_addr(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// Offset of output element 0 of row y for a layout, relative to the image base (the column part is separate).
+__device__ __forceinline__ int64_t row_term(int layout, int y, int dst) {
+  if (layout == KO_LAYOUT_HWC) return static_cast<int64_t>(y) * dst * 3;
+  if (layout == KO_LAYOUT_CHW) return static_cast<int64_t>(y) * dst;
+  return static_cast<int64_t>(y >> 4) * (dst >> 4) * 768 + (y & 15) * 48;  // PATCH16
+}
+
+// The 4 outputs of one item from the staged rows s0 (top) and s1 (bottom).
+template <int MODE>
+__device__ __forceinline__ float4 item_values(const uint8_t* s0, const uint8_t* s1, const int4 (&tap)[4],
+                                              uint32_t chans, int4 yt, const float* slut) {
+  float v[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int4 t = tap[j];
+    const int A = s0[t.x], B = s0[t.y], C = s1[t.x], D = s1[t.y];
+    int q;
+    if (MODE == 0) {
+      const int left = (A * 256 + (C - A) * yt.z + 128) >> 8;
+      const int right = (B * 256 + (D - B) * yt.z + 128) >> 8;
+      q = (left * 256 + (right - left) * t.z + 128) >> 8;
+    } else {
+      const int h0 = A * t.z + B * t.w;
+      const int h1 = C * t.z + D * t.w;
+      q = ((((h0 >> 4) * yt.z) >> 16) + (((h1 >> 4) * yt.w) >> 16) + 2) >> 2;
+    }
+    q = min(max(q, 0), 255);
+    v[j] = slut[(((chans >> (2 * j)) & 3u) << 8) + q];  // RGB channel of element j: 2 bits each
+  }
+  return make_float4(v[0], v[1], v[2], v[3]);
+}
+
+template <int IPT>
+__global__ void __launch_bounds__(kBandThreads) preprocess_band_kernel(const __grid_constant__ BatchParams p,
+                                                                       const float* __restrict__ lut, int dst,
+                                                                       int layout, float* __restrict__ out,
+                                                                       int row_cap, int band) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  float* slut = reinterpret_cast<float*>(smem);  // [3][256]
+  uint8_t* rowbuf = smem + 768 * 4;              // [2 buffers][2 rows][row_cap]
+  const ImageParams& im = p.img[blockIdx.y];
+  const int tid = threadIdx.x;
+  const int y_begin = blockIdx.x * band;
+  const int y_end = min(y_begin + band, dst);
+  if (y_begin >= dst) return;
+  const int row_bytes = static_cast<int>(im.src_w) * 3;
+  const int last = row_bytes - 1;
+  const int rmax = static_cast<int>(im.src_h) - 1;
+  const int n_items = dst * 3 / 4;
+  const int per_ch = dst / 4;
+  const int64_t img_base = static_cast<int64_t>(blockIdx.y) * dst * dst * 3;
+  const int mode = im.mode;
+  const bool vec = im.vec_ok != 0;
+  const int n16 = row_bytes >> 4;
+
+  // Stage the two source rows of output row y into buffer `buf` (vector path: cp.async, 16 bytes per copy);
+  // returns the row's ytab entry, which the compute step of that row needs again.
+  auto stage = [&](int y, int buf) -> int4 {
+    const int4 yt = __ldg(im.ytab + y);
+    const int r0 = min(max(yt.x, 0), rmax), r1 = min(max(yt.y, 0), rmax);
+    const uint8_t* g0 = im.src + static_cast<int64_t>(r0) * im.src_stride;
+    const uint8_t* g1 = im.src + static_cast<int64_t>(r1) * im.src_stride;
+    uint8_t* s0 = rowbuf + (2 * buf) * row_cap;
+    uint8_t* s1 = s0 + row_cap;
+    if (vec) {
+      for (int i = tid; i < n16; i += kBandThreads) {
+        cp_async16(s0 + 16 * i, g0 + 16 * i);
+        cp_async16(s1 + 16 * i, g1 + 16 * i);
+      }
+    } else {
+      for (int i = tid; i < row_bytes; i += kBandThreads) {
+        s0[i] = __ldg(g0 + i);
+        s1[i] = __ldg(g1 + i);
+      }
+    }
+    cp_async_commit();
+    return yt;
+  };
+
+  int4 yt_next = stage(y_begin, 0);
+  for (int i = tid; i < 768; i += kBandThreads) slut[i] = __ldg(lut + i);
+
+  // Per-thread column set-up: clamped taps (l, r), weights, RGB channel and output column offset of each element.
+  int4 tap[IPT][4];
+  uint32_t chans[IPT];
+  float* obase[IPT];
+  bool live[IPT];
+#pragma unroll
+  for (int k = 0; k < IPT; ++k) {
+    const int i = tid + k * kBandThreads;
+    live[k] = i < n_items;
+    chans[k] = 0;
+    int64_t col_off = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tap[k][j] = make_int4(0, 0, 0, 0);
+    if (live[k]) {
+      if (layout == KO_LAYOUT_CHW) {
+        const int c_rgb = i / per_ch, x0 = (i - c_rgb * per_ch) * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          tap[k][j] = __ldg(im.xtab + (x0 + j) * 3 + (2 - c_rgb));
+          chans[k] |= static_cast<uint32_t>(c_rgb) << (2 * j);
+        }
+        col_off = static_cast<int64_t>(c_rgb) * dst * dst + x0;
+      } else {
+        const int o0 = i * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int o = o0 + j, x = o / 3, c_rgb = o - x * 3;
+          tap[k][j] = __ldg(im.xtab + x * 3 + (2 - c_rgb));
+          chans[k] |= static_cast<uint32_t>(c_rgb) << (2 * j);
+        }
+        if (layout == KO_LAYOUT_HWC) {
+          col_off = o0;
+        } else {
+          const int px = o0 / 48;
+          col_off = static_cast<int64_t>(px) * 768 + (o0 - px * 48);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        tap[k][j].x = min(max(tap[k][j].x, 0), last);
+        tap[k][j].y = min(max(tap[k][j].y, 0), last);
+      }
+    }
+    obase[k] = out + img_base + col_off;
+  }
+
+  for (int y = y_begin; y < y_end; ++y) {
+    const int buf = (y - y_begin) & 1;
+    const int4 yt = yt_next;
+    if (y + 1 < y_end) {
+      yt_next = stage(y + 1, buf ^ 1);
+    } else {
+      cp_async_commit();  // empty group keeps the wait count uniform
+    }
+    cp_async_wait_1();
+    __syncthreads();
+    const uint8_t* s0 = rowbuf + (2 * buf) * row_cap;
+    const uint8_t* s1 = s0 + row_cap;
+    const int64_t rt = row_term(layout, y, dst);
+#pragma unroll
+    for (int k = 0; k < IPT; ++k) {
+      if (!live[k]) continue;
+      const float4 v = mode == 0 ? item_values<0>(s0, s1, tap[k], chans[k], yt, slut)
+                                 : item_values<1>(s0, s1, tap[k], chans[k], yt, slut);
+      *reinterpret_cast<float4*>(obase[k] + rt) = v;
+    }
+    __syncthreads();  // buffer `buf` is restaged two rows from now
+  }
+}
+
 int validate_image(const ko_image_desc& d, int64_t dst, const char* who) {
   if (!d.src || !d.xtab || !d.ytab) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": null pointer");
   if (d.src_h < 1 || d.src_w < 1 || d.src_stride < d.src_w * 3 || d.src_w > (1 << 20) || d.src_h > (1 << 20))
@@ -158,8 +332,28 @@ extern "C" int ko_preprocess_batch(const ko_image_desc* images, int n, const flo
     q.vec_ok = ko::aligned16(d.src) && d.src_stride % 16 == 0 && (d.src_w * 3) % 16 == 0;
     row_cap = std::max<int64_t>(row_cap, (d.src_w * 3 + 15) / 16 * 16);
   }
-  const int64_t smem = 2 * row_cap;
   const ko::DeviceInfo& info = ko::device_info();
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t n_items = dst * 3 / 4;
+  if (n_items <= 2 * kBandThreads) {
+    // Band kernel: the largest band (rows per CTA) that still gives every SM about eight CTAs.
+    const int64_t target = 8 * static_cast<int64_t>(info.sm_count);
+    int band = 16;
+    while (band > 1 && n * ((dst + band - 1) / band) < target) band /= 2;
+    const int64_t smem = 768 * 4 + 4 * row_cap;
+    if (smem > info.max_smem_optin) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_preprocess: source rows too wide");
+    dim3 grid(static_cast<unsigned>((dst + band - 1) / band), static_cast<unsigned>(n));
+    auto kern = n_items <= kBandThreads ? preprocess_band_kernel<1> : preprocess_band_kernel<2>;
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e != cudaSuccess) return ko::fail(static_cast<int>(e), "ko_preprocess: cannot enable large shared memory");
+    }
+    kern<<<grid, kBandThreads, smem, st>>>(p, lut, static_cast<int>(dst), layout, out, static_cast<int>(row_cap),
+                                           band);
+    return ko::check_launch("ko_preprocess");
+  }
+  // Wider outputs: one CTA per (output row, image), row pair staged synchronously.
+  const int64_t smem = 2 * row_cap;
   if (smem > info.max_smem_optin) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_preprocess: source rows too wide");
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(preprocess_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -167,7 +361,7 @@ extern "C" int ko_preprocess_batch(const ko_image_desc* images, int n, const flo
     if (e != cudaSuccess) return ko::fail(static_cast<int>(e), "ko_preprocess: cannot enable large shared memory");
   }
   dim3 grid(static_cast<unsigned>(dst), static_cast<unsigned>(n));
-  preprocess_kernel<<<grid, kThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+  preprocess_kernel<<<grid, kThreads, smem, st>>>(
       p, lut, static_cast<int>(dst), layout, out, static_cast<int>(row_cap));
   return ko::check_launch("ko_preprocess");
 }

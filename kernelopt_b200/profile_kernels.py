@@ -8,8 +8,10 @@ Kernels and workloads (per frame of batch B; the algorithmic traffic or flops co
   resln       rows = B*1600, C = 384, x/residual ~ N(0,1); bytes = 4 * rows * 384 * 4
   gemm        GELU(A @ W + b), A [B*1600, 384] ~ N(0,1), W [384, 1536] ~ N(0, 0.02^2); flops = 2*M*384*1536
   deform      value [B,1600,16,16], loc U[-0.05,1.05], softmax aw; bytes = 2,060,800 per frame
-Each timed iteration is bracketed by a write of a 256 MB buffer (larger than the 126 MB L2), outside the
-events, so every launch starts with a cold L2. One JSON line per run. Under ncu, use --iters 1-3.
+Each timed iteration is preceded, outside the events, by a write and a read-back of a 256 MB buffer (larger
+than the 126 MB L2): every launch starts with a cold L2 that holds no dirty lines of the flush (their write-back
+would otherwise be charged to the timed kernel), and a short spin kernel holds the stream while the host enqueues the
+launch, so the events time the GPU's work alone. One JSON line per run. Under ncu, use --iters 1-3.
 """
 from __future__ import annotations
 
@@ -20,7 +22,7 @@ import numpy as np
 import torch
 
 from . import kernels as K
-from .benchutil import measured_peaks
+from .benchutil import hold_stream, measured_peaks
 from .resize_tables import tables
 
 SIZES = [(1080, 1920), (720, 1280), (540, 960)]
@@ -81,6 +83,8 @@ def main():
     times = []
     for _ in range(args.iters):
         flush.fill_(1.0)
+        flush.sum()          # read it back: the fill's dirty lines are written back before the timed launch
+        hold_stream(0.002)   # the host's launch overhead stays outside the events
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         fn()

@@ -90,6 +90,38 @@ def test_preprocess_batch_mixed_sizes(cuda, layout):
     assert np.array_equal(out.cpu().numpy().view(np.uint32), np.stack(refs).view(np.uint32))
 
 
+def test_preprocess_many_frames_use_row_bands(cuda):
+    """16 frames of mixed sizes in one launch: the band kernel gives each CTA several output rows."""
+    lut = gpu_lut(cuda)
+    sizes = [(1080, 1920), (720, 1280), (540, 960), (641, 1279)]
+    items, refs = [], []
+    for i in range(16):
+        h, w = sizes[i % 4]
+        img = frame(h, w, 200 + i, "noise" if i % 2 == 0 else "gradient")
+        mode, xt, yt = RT.tables(w, h)
+        items.append((torch.from_numpy(img).to(cuda), torch.from_numpy(np.array(xt)).to(cuda),
+                      torch.from_numpy(np.array(yt)).to(cuda), mode))
+        refs.append(OR.preprocess(img, layout="patch16"))
+    out = K.preprocess_batch(items, lut, layout="patch16")
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), np.stack(refs).view(np.uint32))
+
+
+@pytest.mark.parametrize("hw,dst,policy", [((1080, 1920), 96, "opencv"), ((500, 333), 160, "reference"),
+                                           ((1080, 1920), 1024, "reference"), ((1080, 1920), 1024, "opencv"),
+                                           ((500, 333), 1024, "reference")])
+def test_preprocess_other_output_sizes(cuda, hw, dst, policy):
+    """Outputs narrower than 342 (one item per thread), and wider than 682 (the one-row-per-CTA kernel)."""
+    h, w = hw
+    lut = gpu_lut(cuda)
+    img = frame(h, w, dst + h)
+    mode, xt, yt = RT.tables(w, h, dst, dst, policy=policy)
+    for layout in ("hwc", "patch16"):
+        g = K.preprocess_gpu(torch.from_numpy(img).to(cuda), torch.from_numpy(np.array(xt)).to(cuda),
+                             torch.from_numpy(np.array(yt)).to(cuda), lut, mode, dst=dst, layout=layout)
+        ref = OR.preprocess(img, dst=dst, policy=policy, layout=layout)
+        assert np.array_equal(g.cpu().numpy().view(np.uint32), ref.view(np.uint32)), (hw, dst, policy, layout)
+
+
 def test_preprocess_rejects_bad_input(cuda):
     lut = gpu_lut(cuda)
     mode, xt, yt = RT.tables(1920, 1080)
@@ -165,6 +197,28 @@ def test_deform_attn_fused_value_layout(cuda, offset):
     loc = loc.reshape(2, 300, 16, 2, 2)
     g = K.deform_attn(t(value), t(loc), t(aw), (40, 40), 16, 16, offset=offset)
     assert_close(g, OK.deform_attn(value, loc, aw, (40, 40), 16, 16, offset), what=f"offset {offset}")
+
+
+def test_deform_attn_large_map(cuda):
+    """A larger map (80x80 tokens, 4 heads) through the two-point kernel."""
+    r = np.random.default_rng(8)
+    value = r.standard_normal((2, 80 * 80, 64)).astype(np.float32)
+    loc = r.uniform(-0.05, 1.05, (2, 50, 4, 2, 2)).astype(np.float32)
+    aw = r.uniform(0, 1, (2, 50, 4, 2)).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    g = K.deform_attn(t(value), t(loc), t(aw), (80, 80), 4, 16)
+    assert_close(g, OK.deform_attn(value, loc, aw, (80, 80), 4, 16, 0), what="large map")
+
+
+def test_deform_attn_three_points_odd_shape(cuda):
+    """The general 4-channel kernel: 2 chunks per head, 3 points, 37 queries and a non-square map."""
+    r = np.random.default_rng(9)
+    value = r.standard_normal((3, 13 * 17, 32)).astype(np.float32)
+    loc = r.uniform(-0.1, 1.1, (3, 37, 3, 3, 2)).astype(np.float32)
+    aw = r.uniform(0, 1, (3, 37, 3, 3)).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    g = K.deform_attn(t(value), t(loc), t(aw), (13, 17), 3, 8, offset=4)
+    assert_close(g, OK.deform_attn(value, loc, aw, (13, 17), 3, 8, 4), what="three points")
 
 
 def test_deform_attn_scalar_path(cuda):

@@ -149,6 +149,19 @@ int ko_linear_gelu_f32(const float* x, const float* w, const float* bias, int64_
 int ko_linear_gelu_f32_noalloc(const float* x, const float* w, const float* bias, int64_t M, int64_t K, int64_t N,
                                float* out, int* dev_status, ko_stream_t stream);
 
+/* --- multi-head attention, fp32 grade (3xTF32 on tcgen05, flash style) ------------------------------------- */
+
+/* o[b, i, h, :] = sum_j softmax_j(scale * q[b, i, h, :] . k[b, j, h, :]) v[b, j, h, :], no mask.
+ * Element (b, i, h, d) of q lives at q + b*q_bstride + i*q_row + h*head_dim + d; k, v and o likewise with their
+ * own strides (in elements), so q, k and v can be column slices of one fused QKV projection.
+ * head_dim 32 or 64; batch, heads <= 65535; every stride a multiple of 4; pointers 16-byte aligned; scale > 0.
+ * Replaces mx.fast.scaled_dot_product_attention at fast_rfdetr/model.py:110 and :119-120 (backbone, windowed and
+ * global layers) and :238 (decoder self-attention). dev_status as for ko_linear_f32_packed. */
+int ko_attention_f32(const float* q, const float* k, const float* v, float* o, int64_t batch, int64_t L,
+                     int64_t heads, int64_t head_dim, int64_t q_bstride, int64_t q_row, int64_t k_bstride,
+                     int64_t k_row, int64_t v_bstride, int64_t v_row, int64_t o_bstride, int64_t o_row, float scale,
+                     int* dev_status, ko_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

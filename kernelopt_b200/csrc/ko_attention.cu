@@ -1,0 +1,521 @@
+// Multi-head scaled-dot-product attention in fp32 grade on the B200 5th-generation tensor cores (tcgen05,
+// kind::tf32, 3xTF32), flash style: the L x L score matrix never leaves the SM.
+//
+//   o[b, i, h, :] = sum_j softmax_j(scale * q[b, i, h, :] . k[b, j, h, :]) v[b, j, h, :]
+//
+// Semantics: the reference's attention calls, mx.fast.scaled_dot_product_attention on head-major q/k/v in the
+// ViT backbone (fast_rfdetr/model.py:107-110 and 119-120, windowed and global layers) and in the decoder's self-attention
+// (self_attn, model.py:232-239, 8 heads of 32), computed in fp32 there. No mask, no dropout.
+//
+// Precision: every operand is split v = hi + lo (hi = tf32_rn(v), lo = tf32_rn(v - hi)) and the tensor cores
+// accumulate hi*hi + hi*lo + lo*hi in fp32 (Ootomo & Yokota's error-compensated 3xTF32). The softmax runs in
+// fp32 registers with the running maximum / running sum of the online (flash) formulation; each key block's
+// P.V product lands in a fresh tensor-memory accumulator and is added into the fp32 output row in registers,
+// so the long sum over keys is a plain fp32 register sum, not a tensor-core accumulation.
+//
+// Kernel structure: one CTA per (128-query tile, head, batch item); 13 warps.
+//   warp 0      allocates tensor memory; one lane issues the MMAs:
+//                 S  = Q K_j^T      (M 128, N 128 keys, K = head dim;  A, B in shared memory)
+//                 O_j = P_j V_j     (M 128, N = head dim, K = 128 keys; A = P in tensor memory, B in shared)
+//   warps 1-4   softmax + output: one thread per query row. Reads S from tensor memory, updates the row's running
+//               max / sum, writes P (hi and lo) back into tensor memory for the P.V MMA, then adds O_j into the
+//               output row it keeps in registers. At the end divides by the sum and stores the row.
+//   warps 5-12  loaders: q, k and v rows straight from global memory (128-bit loads; warps 5-8 stream k, 9-12
+//               stream v, each holding the next key block in registers while the current one is in use), split
+//               into hi / lo and written into shared memory in the MMA's 128-byte-swizzled K-major layout. v is
+//               written transposed (head dim x keys), the K-major form of the P.V product's B operand.
+// Tensor memory (512 columns): two S / P_hi buffers [0,256), P_lo [256,384), two O_j buffers of HD columns from
+// 384. With two S buffers the tensor cores compute S_{j+1} while the softmax warps work on block j.
+// Every wait on an mbarrier is bounded (2 s); on timeout the CTA stops, drains its MMAs, frees tensor memory and
+// reports KO_ERR_DEVICE_TIMEOUT through dev_status.
+#include <algorithm>
+#include <climits>
+#include <string>
+
+#include "ko_common.cuh"
+
+namespace {
+
+using namespace kodev;
+
+constexpr int BQ = 128;    // query rows per CTA (MMA M)
+constexpr int BKEY = 128;  // keys per block (MMA N of S, K of P.V)
+constexpr int kLoadWarp0 = 5;
+constexpr int kLoadThreads = 256;
+constexpr int kThreads = 13 * 32;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0;      // two S / P_hi buffers of 128 columns
+constexpr uint32_t kColPlo = 256;  // P_lo, 128 columns
+constexpr uint32_t kColO = 384;    // two O_j buffers of HD columns
+
+struct AttnArgs {
+  const float* q;
+  const float* k;
+  const float* v;
+  float* o;
+  int64_t q_bstride, k_bstride, v_bstride, o_bstride;  // elements between consecutive batch items
+  int q_row, k_row, v_row, o_row;                      // elements between consecutive tokens
+  int L, n_kblocks;
+  float scale_log2;  // softmax scale * log2(e): exponentials are taken as exp2
+  int* dev_status;
+};
+
+template <int HD>
+struct AttnCfg {
+  static constexpr int kKB = HD / 32;                          // 128-byte k-blocks of a q / k row
+  static constexpr uint32_t kQBytes = BQ * HD * 4;             // one of Q_hi / Q_lo
+  static constexpr uint32_t kKBytes = BKEY * HD * 4;           // one of K_hi / K_lo
+  static constexpr uint32_t kVBytes = HD * BKEY * 4;           // one of Vt_hi / Vt_lo
+  static constexpr uint32_t kOffQlo = kQBytes;
+  static constexpr uint32_t kOffKhi = 2 * kQBytes;
+  static constexpr uint32_t kOffKlo = kOffKhi + kKBytes;
+  static constexpr uint32_t kOffVhi = kOffKlo + kKBytes;
+  static constexpr uint32_t kOffVlo = kOffVhi + kVBytes;
+  static constexpr uint32_t kOffBars = kOffVlo + kVBytes;
+  // At least 120 KB even where the tiles need less (head dim 32), so that one CTA per SM holds all 512 tensor-
+  // memory columns and no second CTA waits in tcgen05.alloc.
+  static constexpr size_t kSmemNeed = 1024 + kOffBars + 256;
+  static constexpr size_t kSmemBytes = kSmemNeed > 120 * 1024 ? kSmemNeed : 120 * 1024;
+  static constexpr int kQChunks = BQ * HD / 4 / kLoadThreads;   // float4 per loader thread for a q tile
+  static constexpr int kKChunks = BKEY * HD / 4 / kLoadThreads;  // ... for a k or v tile
+  static_assert(HD == 32 || HD == 64, "head dim 32 or 64");
+};
+
+// Byte offset of 16-byte chunk `c` (0..7) of row `r` in a K-major tile of 128-byte rows, 128-byte swizzle.
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+  return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::tf32, one CTA (A: M lanes x K columns of tensor memory).
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void split_tf32(float v, float& hi, float& lo) {
+  hi = __uint_as_float(f32_to_tf32_rna(v));
+  lo = __uint_as_float(f32_to_tf32_rna(v - hi));
+}
+
+// 32 lanes x 16 consecutive 32-bit columns, load and store.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait_regs16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// mbarrier wait whose result is the same in every lane of the warp (the warp then runs .sync.aligned tcgen05
+// operations together, or leaves its loop together).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const bool ok = mbar_wait(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// 2^x by the MUFU (ex2.approx, relative error below 2^-22 over the range used here: x <= 0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const AttnArgs a) {
+  using C = AttnCfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
+  uint64_t* q_ready = bars + 0;   // q tile written          (8 loader warps)
+  uint64_t* k_full = bars + 1;    // k tile written          (4 k-loader warps)
+  uint64_t* k_empty = bars + 2;   // S MMAs done with it     (1 commit)
+  uint64_t* v_full = bars + 3;    // v tile written          (4 v-loader warps)
+  uint64_t* v_empty = bars + 4;   // P.V MMAs done with it   (1 commit)
+  uint64_t* s_full = bars + 5;    // S_j complete, x2        (1 commit)
+  uint64_t* p_full = bars + 7;    // P_j written             (4 softmax warps)
+  uint64_t* o_full = bars + 8;    // O_j complete, x2        (1 commit)
+  uint64_t* o_empty = bars + 10;  // O_j consumed, x2        (4 softmax warps)
+  uint64_t* mma_done = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * BQ;
+  const int nkb = a.n_kblocks;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_ready, 8);
+    mbar_init(k_full, 4);
+    mbar_init(k_empty, 1);
+    mbar_init(v_full, 4);
+    mbar_init(v_empty, 1);
+    mbar_init(p_full, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- MMA issuer ----------------
+    // Order on the tensor pipe: S_0, then per block j: S_{j+1} (into the other S buffer, overlapping softmax_j),
+    // P_j.V_j. S_{j+1} reuses the buffer of P_{j-1}, so it waits for P_{j-1}.V_{j-1} to complete.
+    if (lane == 0) {
+      // Descriptors are built once; an MMA's operand is its tile's descriptor plus the byte offset / 16 (the
+      // start-address field; shared addresses stay below 2^18 bytes, so the field cannot overflow).
+      const uint32_t sb = smem_addr(smem);
+      constexpr uint32_t idesc_o = idesc_tf32(BQ, HD);
+      const uint64_t dq_hi = smem_desc_k_sw128(sb), dq_lo = smem_desc_k_sw128(sb + C::kOffQlo);
+      const uint64_t dk_hi = smem_desc_k_sw128(sb + C::kOffKhi), dk_lo = smem_desc_k_sw128(sb + C::kOffKlo);
+      const uint64_t dv_hi = smem_desc_k_sw128(sb + C::kOffVhi), dv_lo = smem_desc_k_sw128(sb + C::kOffVlo);
+      // A short last key block (e.g. 17 of the 401 keys of a window) gets MMAs only as wide / deep as its keys:
+      // N = keys rounded up to 16 for S, K = keys rounded up to 8 for P.V.
+      auto keys_of = [&](int j) { return min(BKEY, a.L - j * BKEY); };
+      auto issue_s = [&](int j) {  // S_j = Q K_j^T into S buffer j & 1
+        const uint32_t d = tmem + kColS + static_cast<uint32_t>(j & 1) * BKEY;
+        const uint32_t idesc_s = idesc_tf32(BQ, (keys_of(j) + 15) & ~15);
+#pragma unroll 1
+        for (int s = 0; s < C::kKB * 4; ++s) {  // 8-wide k-steps over the head dimension
+          const uint64_t off = static_cast<uint64_t>(((s >> 2) * (BQ * 128) + (s & 3) * 32) >> 4);
+          mma_tf32(d, dq_lo + off, dk_hi + off, idesc_s, s == 0 ? 0u : 1u);
+          mma_tf32(d, dq_hi + off, dk_lo + off, idesc_s, 1u);
+          mma_tf32(d, dq_hi + off, dk_hi + off, idesc_s, 1u);
+        }
+        mma_commit(&s_full[j & 1]);
+        mma_commit(k_empty);
+      };
+      bool ok = mbar_wait(q_ready, 0, abort_flag) && mbar_wait(k_full, 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; j < nkb && ok; ++j) {
+        if (j + 1 < nkb) {
+          if (!mbar_wait(k_full, static_cast<uint32_t>(j + 1) & 1u, abort_flag)) break;
+          if (j >= 1 && !mbar_wait(&o_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag)) break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
+        // O_j = P_j V_j into O buffer j & 1, once P_j is written, V_j landed and the buffer was consumed
+        if (!mbar_wait(p_full, static_cast<uint32_t>(j) & 1u, abort_flag) ||
+            !mbar_wait(v_full, static_cast<uint32_t>(j) & 1u, abort_flag) ||
+            !mbar_wait(&o_empty[j & 1], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, abort_flag))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem + kColO + static_cast<uint32_t>(j & 1) * HD;
+        const uint32_t p_hi = tmem + kColS + static_cast<uint32_t>(j & 1) * BKEY;
+        const int ksteps = (keys_of(j) + 7) >> 3;
+#pragma unroll 1
+        for (int kk = 0; kk < ksteps; ++kk) {  // 8 keys per k-step
+          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
+          const uint32_t phi = p_hi + 8 * kk, plo = tmem + kColPlo + 8 * kk;
+          mma_tf32_ts(d, plo, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
+          mma_tf32_ts(d, phi, dv_lo + off, idesc_o, 1u);
+          mma_tf32_ts(d, phi, dv_hi + off, idesc_o, 1u);
+        }
+        mma_commit(&o_full[j & 1]);
+        mma_commit(v_empty);
+      }
+      // Drain: every MMA this thread issued completes before tensor memory is released.
+      mma_commit(mma_done);
+      volatile int never = 0;
+      if (!mbar_wait(mma_done, 0, &never)) *abort_flag = 1;
+    }
+  } else if (warp < kLoadWarp0) {
+    // ---------------- softmax + output, one thread per query row ----------------
+    // Block j: max of S_j (pass 1); then, once P_{j-1}.V_{j-1} is complete, O += that block's product (which
+    // also frees the P_lo columns); then P_j = exp2(S_j * c - m) as hi / lo into tensor memory (pass 2).
+    const int quad = warp & 3;  // tensor-memory lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    float o[HD];
+#pragma unroll
+    for (int d = 0; d < HD; ++d) o[d] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    bool ok = true;
+    auto add_block = [&](int jb, float alpha) -> bool {  // o = o * alpha + O_jb
+      if (!warp_wait(&o_full[jb & 1], static_cast<uint32_t>(jb >> 1) & 1u, abort_flag)) return false;
+      tc_fence_after();
+      const uint32_t ob = trow + kColO + static_cast<uint32_t>(jb & 1) * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 16; ++c) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(ob + 16 * c, r);
+        tmem_ld_wait_regs16(r);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) o[16 * c + e] = fmaf(o[16 * c + e], alpha, __uint_as_float(r[e]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[jb & 1]);
+      return true;
+    };
+    for (int j = 0; j < nkb; ++j) {
+      if (!warp_wait(&s_full[j & 1], static_cast<uint32_t>(j >> 1) & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t srow = trow + kColS + static_cast<uint32_t>(j & 1) * BKEY;
+      const int valid = min(BKEY, a.L - j * BKEY);
+      const int chunks = (valid + 15) >> 4;  // 16-column chunks that hold keys of this block
+      float mb = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < chunks; ++c) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(srow + 16 * c, r);
+        tmem_ld_wait_regs16(r);
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (16 * c + e < valid) mb = fmaxf(mb, __uint_as_float(r[e]));
+      }
+      const float m_new = fmaxf(m, mb * a.scale_log2);
+      const float alpha = fast_exp2(m - m_new);
+      if (j >= 1 && !add_block(j - 1, alpha_prev)) {
+        ok = false;
+        break;
+      }
+      float ls = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < chunks; ++c) {
+        uint32_t r[16], lo[16];
+        tmem_ld_32x32b_x16(srow + 16 * c, r);
+        tmem_ld_wait_regs16(r);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p = (16 * c + e < valid) ? fast_exp2(fmaf(__uint_as_float(r[e]), a.scale_log2, -m_new)) : 0.f;
+          ls += p;
+          float phi, plo;
+          split_tf32(p, phi, plo);
+          r[e] = __float_as_uint(phi);
+          lo[e] = __float_as_uint(plo);
+        }
+        tmem_st_32x32b_x16(srow + 16 * c, r);
+        tmem_st_32x32b_x16(trow + kColPlo + 16 * c, lo);
+      }
+      tmem_st_wait();
+      l = l * alpha + ls;
+      m = m_new;
+      alpha_prev = alpha;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok && !add_block(nkb - 1, alpha_prev)) ok = false;
+    const int qi = q0 + row;
+    if (ok && qi < a.L) {
+      const float inv = 1.0f / l;
+      float4* dst = reinterpret_cast<float4*>(a.o + static_cast<int64_t>(b) * a.o_bstride +
+                                              static_cast<int64_t>(qi) * a.o_row + h * HD);
+#pragma unroll
+      for (int d = 0; d < HD / 4; ++d)
+        dst[d] = make_float4(o[4 * d] * inv, o[4 * d + 1] * inv, o[4 * d + 2] * inv, o[4 * d + 3] * inv);
+    }
+  } else {
+    // ---------------- loaders ----------------
+    // All 8 warps write the q tile; then warps 5-8 stream the k tiles and warps 9-12 the v tiles, each group
+    // holding its next tile in registers while the current one is in use.
+    const int t = threadIdx.x - kLoadWarp0 * 32;  // 0..255
+    constexpr int Q4 = HD / 4;                   // float4 per row
+    const float* qb = a.q + static_cast<int64_t>(b) * a.q_bstride + h * HD;
+    {
+      float4 reg[C::kQChunks];
+#pragma unroll
+      for (int i = 0; i < C::kQChunks; ++i) {
+        const int idx = i * kLoadThreads + t, r = idx / Q4, c = idx % Q4, tok = q0 + r;
+        reg[i] = tok < a.L ? __ldg(reinterpret_cast<const float4*>(qb + static_cast<int64_t>(tok) * a.q_row) + c)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < C::kQChunks; ++i) {
+        const int idx = i * kLoadThreads + t, r = idx / Q4, c = idx % Q4;
+        const uint32_t off = (c >> 3) * (BQ * 128) + sw128(r, c & 7);
+        float4 hi, lo;
+        split_tf32(reg[i].x, hi.x, lo.x);
+        split_tf32(reg[i].y, hi.y, lo.y);
+        split_tf32(reg[i].z, hi.z, lo.z);
+        split_tf32(reg[i].w, hi.w, lo.w);
+        *reinterpret_cast<float4*>(smem + off) = hi;
+        *reinterpret_cast<float4*>(smem + C::kOffQlo + off) = lo;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+    }
+    constexpr int kGroup = kLoadThreads / 2;       // 128 threads per group
+    constexpr int kTileChunks = BKEY * HD / 4 / kGroup;
+    const int g = t & (kGroup - 1);
+    float4 reg[kTileChunks];
+    if (t < kGroup) {
+      // k tiles: row-major chunks (a warp reads whole rows), stored K-major with the 128-byte swizzle
+      const float* kbp = a.k + static_cast<int64_t>(b) * a.k_bstride + h * HD;
+      auto load = [&](int j) {
+#pragma unroll
+        for (int i = 0; i < kTileChunks; ++i) {
+          const int idx = i * kGroup + g, kr = j * BKEY + idx / Q4, kc = idx % Q4;
+          reg[i] = kr < a.L ? __ldg(reinterpret_cast<const float4*>(kbp + static_cast<int64_t>(kr) * a.k_row) + kc)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      };
+      load(0);
+      for (int j = 0; j < nkb; ++j) {
+        if (!mbar_wait(k_empty, (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag)) break;
+#pragma unroll
+        for (int i = 0; i < kTileChunks; ++i) {
+          const int idx = i * kGroup + g, r = idx / Q4, c = idx % Q4;
+          const uint32_t off = (c >> 3) * (BKEY * 128) + sw128(r, c & 7);
+          float4 hi, lo;
+          split_tf32(reg[i].x, hi.x, lo.x);
+          split_tf32(reg[i].y, hi.y, lo.y);
+          split_tf32(reg[i].z, hi.z, lo.z);
+          split_tf32(reg[i].w, hi.w, lo.w);
+          *reinterpret_cast<float4*>(smem + C::kOffKhi + off) = hi;
+          *reinterpret_cast<float4*>(smem + C::kOffKlo + off) = lo;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(k_full);
+        if (j + 1 < nkb) load(j + 1);
+      }
+    } else {
+      // v tiles: a warp reads 32 consecutive keys of one 4-wide column group and writes them transposed
+      // (head dim x keys, K-major, 128-byte swizzle): every scalar store of the warp fills one 128-byte row.
+      const float* vbp = a.v + static_cast<int64_t>(b) * a.v_bstride + h * HD;
+      auto load = [&](int j) {
+#pragma unroll
+        for (int i = 0; i < kTileChunks; ++i) {
+          const int idx = i * kGroup + g, vr = j * BKEY + (idx & (BKEY - 1)), vc = idx / BKEY;
+          reg[i] = vr < a.L ? __ldg(reinterpret_cast<const float4*>(vbp + static_cast<int64_t>(vr) * a.v_row) + vc)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      };
+      load(0);
+      for (int j = 0; j < nkb; ++j) {
+        if (!mbar_wait(v_empty, (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag)) break;
+#pragma unroll
+        for (int i = 0; i < kTileChunks; ++i) {
+          const int idx = i * kGroup + g, key = idx & (BKEY - 1), dq = idx / BKEY;
+          const uint32_t base = (key >> 5) * (HD * 128) + ((key & 3) << 2);
+          const float* src = reinterpret_cast<const float*>(&reg[i]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int d = 4 * dq + e;
+            const uint32_t off = base + sw128(d, (key & 31) >> 2);
+            float hi, lo;
+            split_tf32(src[e], hi, lo);
+            *reinterpret_cast<float*>(smem + C::kOffVhi + off) = hi;
+            *reinterpret_cast<float*>(smem + C::kOffVlo + off) = lo;
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(v_full);
+        if (j + 1 < nkb) load(j + 1);
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag && a.dev_status) atomicExch(a.dev_status, KO_ERR_DEVICE_TIMEOUT);
+}
+
+}  // namespace
+
+extern "C" int ko_attention_f32(const float* q, const float* k, const float* v, float* o, int64_t batch, int64_t L,
+                                int64_t heads, int64_t head_dim, int64_t q_bstride, int64_t q_row,
+                                int64_t k_bstride, int64_t k_row, int64_t v_bstride, int64_t v_row,
+                                int64_t o_bstride, int64_t o_row, float scale, int* dev_status, ko_stream_t stream) {
+  const char* who = "ko_attention_f32";
+  if (head_dim != 32 && head_dim != 64)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": head_dim must be 32 or 64");
+  if (batch < 0 || L < 0 || heads < 1 || batch > 65535 || heads > 65535 || L > (int64_t(1) << 30))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": bad batch / length / heads");
+  if (batch == 0 || L == 0) return KO_OK;
+  if (!q || !k || !v || !o) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": null pointer");
+  const int64_t strides[8] = {q_bstride, q_row, k_bstride, k_row, v_bstride, v_row, o_bstride, o_row};
+  for (int64_t st : strides)
+    if (st < 0 || st % 4 != 0 || st > INT32_MAX * int64_t(4))
+      return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": strides must be non-negative multiples of 4");
+  if (q_row > INT32_MAX || k_row > INT32_MAX || v_row > INT32_MAX || o_row > INT32_MAX)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": row stride too large");
+  if (heads * head_dim > q_row || heads * head_dim > k_row || heads * head_dim > v_row || heads * head_dim > o_row)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": a row must hold heads * head_dim values");
+  if (!ko::aligned16(q) || !ko::aligned16(k) || !ko::aligned16(v) || !ko::aligned16(o))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": pointers must be 16-byte aligned");
+  if (!(scale > 0.0f)) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": scale must be positive");
+  AttnArgs a;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.o = o;
+  a.q_bstride = q_bstride;
+  a.k_bstride = k_bstride;
+  a.v_bstride = v_bstride;
+  a.o_bstride = o_bstride;
+  a.q_row = static_cast<int>(q_row);
+  a.k_row = static_cast<int>(k_row);
+  a.v_row = static_cast<int>(v_row);
+  a.o_row = static_cast<int>(o_row);
+  a.L = static_cast<int>(L);
+  a.n_kblocks = static_cast<int>((L + BKEY - 1) / BKEY);
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.dev_status = dev_status;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid(static_cast<unsigned>((L + BQ - 1) / BQ), static_cast<unsigned>(heads), static_cast<unsigned>(batch));
+  const ko::DeviceInfo& info = ko::device_info();
+  if (head_dim == 64) {
+    using C = AttnCfg<64>;
+    if (static_cast<int64_t>(C::kSmemBytes) > info.max_smem_optin)
+      return ko::fail(KO_ERR_UNSUPPORTED, std::string(who) + ": not enough shared memory on this device");
+    cudaError_t e = cudaFuncSetAttribute(attention_tf32x3_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(C::kSmemBytes));
+    if (e != cudaSuccess) return ko::fail(static_cast<int>(e), std::string(who) + ": cudaFuncSetAttribute failed");
+    attention_tf32x3_kernel<64><<<grid, kThreads, C::kSmemBytes, st>>>(a);
+  } else {
+    using C = AttnCfg<32>;
+    cudaError_t e = cudaFuncSetAttribute(attention_tf32x3_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(C::kSmemBytes));
+    if (e != cudaSuccess) return ko::fail(static_cast<int>(e), std::string(who) + ": cudaFuncSetAttribute failed");
+    attention_tf32x3_kernel<32><<<grid, kThreads, C::kSmemBytes, st>>>(a);
+  }
+  return ko::check_launch(who);
+}

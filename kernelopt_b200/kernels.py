@@ -4,6 +4,7 @@
     preprocess_gpu(img_u8, xtab, ytab, lut, mode, dst=640) -> [dst,dst,3]      kernels.py:106
     deform_attn(value, loc, aw, grid_hw, nh, hd, offset=0) -> [B,NQ,NH*HD]     kernels.py:165
     linear_gelu_f32(x, w, bias) -> [..., N]                                    kernels.py:271
+plus attention(q, k, v, heads, scale), which replaces the reference's mx.fast.scaled_dot_product_attention calls.
 
 Every call goes to libkernelopt.so (hand-written sm_100a CUDA) on the caller's current CUDA stream. Outputs
 are freshly allocated; inputs are read-only and must be contiguous float32 (uint8/int32 for preprocessing)
@@ -160,6 +161,35 @@ def deform_attn(value, loc, aw, grid_hw, nh, hd, offset=0):
     out = torch.empty((b, nq, nh * hd), dtype=torch.float32, device=value.device)
     call("ko_deform_attn", value.data_ptr(), loc.data_ptr(), aw.data_ptr(), b, nq, nh, hd, npts, gh, gw, row,
          offset, out.data_ptr(), _stream())
+    return out
+
+
+# ---- multi-head attention ----
+def attention(q, k, v, heads, scale, out=None):
+    """softmax(scale * q k^T) v for every head, fp32 grade (the 3xTF32 tcgen05 flash kernel; the reference uses
+    mx.fast.scaled_dot_product_attention, model.py:110, :119-120, :238).
+
+    q, k, v: [B, L, heads * head_dim] float32 CUDA tensors (head_dim 32 or 64) whose last dimension is contiguous
+    — column slices of one fused QKV projection need no copy. Returns [B, L, heads * head_dim] contiguous, or
+    writes `out` (same shape, last dimension contiguous)."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor (there is no CPU path)")
+        if t.dtype != torch.float32 or t.dim() != 3 or t.stride(2) != 1:
+            raise ValueError(f"{name} must be float32 [B, L, heads*head_dim] with a contiguous last dimension")
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k and v must have the same shape")
+    b, n, width = q.shape
+    hd = width // heads
+    if hd * heads != width or hd not in (32, 64):
+        raise ValueError("head_dim = width / heads must be 32 or 64")
+    if out is None:
+        out = torch.empty((b, n, width), dtype=torch.float32, device=q.device)
+    elif tuple(out.shape) != (b, n, width) or out.dtype != torch.float32 or out.stride(2) != 1:
+        raise ValueError("out must be float32 [B, L, heads*head_dim] with a contiguous last dimension")
+    call("ko_attention_f32", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, n, heads, hd,
+         q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1), out.stride(0), out.stride(1),
+         float(scale), status_word(q.device).data_ptr(), _stream())
     return out
 
 

@@ -8,8 +8,10 @@ Call sites of the reference's kernels (model.py:122, 125, 131, 226) use the same
   deform_attn          decoder cross-attention sampling, on the one fused [B,1600,1024] value projection
 Every other dense layer (QKV, out-proj, fc2, the patch embedding, the projector's 1x1 and im2col'd 3x3 convs,
 the decoder linears) runs on the same fp32-grade tcgen05 GEMM; only the layers whose output width is not a
-multiple of 4 (11 classes, 4 box coordinates) use torch's fp32 matmul. Attention (SDPA), LayerNorms outside
-the fused sites, SiLU, softmax and top-300 are torch ops in fp32 with TF32 disabled.
+multiple of 4 (11 classes, 4 box coordinates) use torch's fp32 matmul. Attention — the backbone's windowed and
+global self-attention and the decoder's self-attention (the reference's mx.fast.scaled_dot_product_attention) — runs
+on the fp32-grade 3xTF32 tcgen05 flash-attention kernel, straight on column slices of the fused QKV projection.
+LayerNorms outside the fused sites, SiLU, softmax and top-300 are torch ops in fp32 with TF32 disabled.
 
 The input is the patch layout the preprocessing kernel writes (PATCH16: [B, 1600, 768]), which makes the
 16x16/16 patch-embedding convolution one GEMM; NHWC [B, 640, 640, 3] (the reference's input) is accepted too.
@@ -176,10 +178,9 @@ class RFDETR:
         """model.py:113-132: attention, residual+LN, fc1+GELU, fc2, residual+LN (next layer's norm1)."""
         n, L, _ = h.shape
         nb, Lb = (b, 4 * L) if i in FULL_ATTN else (n, L)                                      # global: merge windows
-        qkv = lyr["qkv"](y.reshape(nb * Lb, C)).reshape(nb, Lb, 3, HEADS, C // HEADS)
-        q, k, v = (qkv[:, :, j].transpose(1, 2) for j in range(3))                             # [nb, 6, Lb, 64]
-        o = F.scaled_dot_product_attention(q, k, v, scale=1 / math.sqrt(C // HEADS))
-        o = lyr["out"](o.transpose(1, 2).reshape(n * L, C)).reshape(n, L, C)
+        qkv = lyr["qkv"](y.reshape(nb * Lb, C)).reshape(nb, Lb, 3 * C)                         # q | k | v columns
+        o = K.attention(qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:], HEADS, 1 / math.sqrt(C // HEADS))
+        o = lyr["out"](o.reshape(n * L, C)).reshape(n, L, C)
         w2, b2, e2 = lyr["norm2"]
         h, y = K.residual_layernorm(h, o, lyr["out_b"], lyr["ls1"], w2, b2, e2)
         m = K.linear(y, lyr["fc1"], "gelu")
@@ -247,11 +248,10 @@ class RFDETR:
         values = self.vproj(memory)                                                              # [B, 1600, 1024]
         hd = D_MODEL // SA_HEADS
         for i, lyr in enumerate(self.dec):
-            qk = lyr["qk"](tgt + qpos).reshape(b, N_QUERIES, 2, SA_HEADS, hd)
-            v = lyr["v"](tgt).reshape(b, N_QUERIES, SA_HEADS, hd).transpose(1, 2)
-            o = F.scaled_dot_product_attention(qk[:, :, 0].transpose(1, 2), qk[:, :, 1].transpose(1, 2), v,
-                                               scale=1 / math.sqrt(hd))
-            sa = lyr["out"](o.transpose(1, 2).reshape(b, N_QUERIES, D_MODEL))
+            qk = lyr["qk"](tgt + qpos).reshape(b, N_QUERIES, 2 * D_MODEL)                      # q | k columns
+            v = lyr["v"](tgt).reshape(b, N_QUERIES, D_MODEL)
+            o = K.attention(qk[..., :D_MODEL], qk[..., D_MODEL:], v, SA_HEADS, 1 / math.sqrt(hd))
+            sa = lyr["out"](o)
             tgt = self._add_ln(tgt, sa, lyr["norm1"])
             oa = lyr["offaw"](tgt + qpos)                                                         # [B, 300, 96]
             off = oa[..., :CA_HEADS * CA_POINTS * 2].reshape(b, N_QUERIES, CA_HEADS, CA_POINTS, 2)

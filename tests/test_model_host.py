@@ -42,6 +42,14 @@ def _deform(value, loc, aw, grid_hw, nh, hd, offset=0):
     return torch.from_numpy(OKn.deform_attn(value.numpy(), loc.numpy(), aw.numpy(), grid_hw, nh, hd, offset))
 
 
+def _attention(q, k, v, heads, scale, out=None):
+    b, n, w = q.shape
+    hd = w // heads
+    qh, kh, vh = (t.reshape(b, n, heads, hd).transpose(1, 2) for t in (q, k, v))
+    p = torch.softmax((qh @ kh.transpose(-1, -2)) * scale, dim=-1)
+    return (p @ vh).transpose(1, 2).reshape(b, n, w)
+
+
 @pytest.fixture()
 def cpu_model(monkeypatch):
     import kernelopt_b200.kernels as K
@@ -50,6 +58,7 @@ def cpu_model(monkeypatch):
     monkeypatch.setattr(K, "linear", _linear)
     monkeypatch.setattr(K, "residual_layernorm", _rln)
     monkeypatch.setattr(K, "deform_attn", _deform)
+    monkeypatch.setattr(K, "attention", _attention)
     monkeypatch.setattr(K, "status_word", lambda *a: None)
     w = random_weights(0)
 

@@ -33,6 +33,14 @@ WORKLOAD = ("RF-DETR-Medium fp32 inference on seeded 1920x1080 uint8 BGR frames:
             "projector + top-300 selection + 4-layer deformable decoder + heads, random-init weights (seed 0)")
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per GEMM launch, mean over the 95 GEMM launches of
+# one step, from one ncu capture of this benchmark at 16 frames per step:
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --cache-control none
+#       --clock-control none -k regex:gemm_tf32x3 -c 95 python bench.py --batch 16 --steps 1 --warmup 3
+# (9258 MB over the 95 launches; the algorithmic bytes of the same launches are 9905 MB).
+GEMM_TRAFFIC_PER_LAUNCH = {16: 97.45e6}
+
+
 def frames_for(rank: int, n: int) -> np.ndarray:
     rng = np.random.default_rng(1000 + rank)
     return rng.integers(0, 256, (n, H, W, 3), dtype=np.uint8)
@@ -115,11 +123,16 @@ def instrumented_step(det, runner_x, items, K):
     from kernelopt_b200 import _lib
     from kernelopt_b200.benchutil import EventTimer, hold_stream
 
-    timers = {n: EventTimer() for n in ("gemm_tf32x3", "residual_layernorm", "deform_attn", "preprocess")}
-    orig = {n: getattr(K, n) for n in ("linear", "residual_layernorm", "deform_attn", "preprocess_batch")}
+    timers = {n: EventTimer() for n in ("gemm_tf32x3", "attention_tf32x3", "residual_layernorm", "deform_attn",
+                                         "preprocess")}
+    orig = {n: getattr(K, n) for n in ("linear", "attention", "residual_layernorm", "deform_attn", "preprocess_batch")}
 
     def gemm_work(x, pw, act=None, out=None):
         return 2.0 * (x.numel() // pw.k) * pw.k * pw.n
+
+    def attn_work(q, k, v, heads, scale, out=None):
+        b, n, w = q.shape
+        return 4.0 * b * n * n * w                       # QK^T and PV, all heads
 
     def ln_work(h, o, *a, **k):
         return 16.0 * h.numel()                          # read h, o; write h_out, y (fp32)
@@ -133,6 +146,7 @@ def instrumented_step(det, runner_x, items, K):
         return float(sum(img.numel() for img, *_ in items_) + len(items_) * dst * dst * 3 * 4)
 
     K.linear = timers["gemm_tf32x3"].wrap(orig["linear"], gemm_work)
+    K.attention = timers["attention_tf32x3"].wrap(orig["attention"], attn_work)
     K.residual_layernorm = timers["residual_layernorm"].wrap(orig["residual_layernorm"], ln_work)
     K.deform_attn = timers["deform_attn"].wrap(orig["deform_attn"], deform_work)
     K.preprocess_batch = timers["preprocess"].wrap(orig["preprocess_batch"], pre_work)
@@ -150,7 +164,7 @@ def instrumented_step(det, runner_x, items, K):
     out = {}
     for n, t in timers.items():
         secs, work, cnt = t.total()
-        out[n] = (secs, work, cnt, "flop" if n == "gemm_tf32x3" else "byte")
+        out[n] = (secs, work, cnt, "flop" if n in ("gemm_tf32x3", "attention_tf32x3") else "byte")
     return out, launches
 
 
@@ -243,7 +257,8 @@ def run_ours(args, rank: int, world: int):
     dom = max(kernels, key=lambda n: kernels[n]["ms_per_step"])
     dk = kernels[dom]
     roofline = {"kernel": dom, "bound": dk["bound"], "achieved": dk["achieved"], "peak": dk["peak"],
-                "unit": dk["unit"], "frac": dk["frac"], "traffic": None,
+                "unit": dk["unit"], "frac": dk["frac"], "traffic": GEMM_TRAFFIC_PER_LAUNCH.get(B) if dom == "gemm_tf32x3"
+                else None, "traffic_unit": "bytes per launch (ncu dram read + write, mean over the step's launches)",
                 "peak_source": ("3xTF32 ceiling = measured bf16 dense / 6 (" + peaks["source"] + ")"
                                 if dk["bound"] == "tensor" else f"{peaks['source']} HBM copy bandwidth"),
                 "step_share_eager": dk["ms_per_step"] / (1e3 * secs / args.steps)}

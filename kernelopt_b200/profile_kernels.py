@@ -8,6 +8,9 @@ Kernels and workloads (per frame of batch B; the algorithmic traffic or flops co
   resln       rows = B*1600, C = 384, x/residual ~ N(0,1); bytes = 4 * rows * 384 * 4
   gemm        GELU(A @ W + b), A [B*1600, 384] ~ N(0,1), W [384, 1536] ~ N(0, 0.02^2); flops = 2*M*384*1536
   deform      value [B,1600,16,16], loc U[-0.05,1.05], softmax aw; bytes = 2,060,800 per frame
+  attn        the backbone's global attention: B frames x 1604 tokens x 6 heads x 64, q/k/v column slices of
+              one [B, 1604, 1152] projection ~ N(0,1); flops = 4 * B * 6 * 1604^2 * 64
+  attn_win    the windowed attention: 4B windows x 401 tokens x 6 heads x 64; flops = 4 * 4B * 6 * 401^2 * 64
 Each timed iteration is preceded, outside the events, by a write and a read-back of a 256 MB buffer (larger
 than the 126 MB L2): every launch starts with a cold L2 that holds no dirty lines of the flush (their write-back
 would otherwise be charged to the timed kernel), and a short spin kernel holds the stream while the host enqueues the
@@ -63,12 +66,17 @@ def setup(kernel: str, b: int, dev):
         loc = (torch.rand(b, 300, 16, 2, 2, generator=g) * 1.1 - 0.05).to(dev)
         aw = torch.softmax(torch.randn(b, 300, 16, 2, generator=g), -1).to(dev)
         return (lambda: K.deform_attn(value, loc, aw, (40, 40), 16, 16)), 2060800.0 * b, "byte"
+    if kernel in ("attn", "attn_win"):
+        nb, n = (b, 1604) if kernel == "attn" else (4 * b, 401)
+        qkv = torch.randn(nb, n, 1152, generator=g).to(dev)
+        q, k, v = qkv[..., :384], qkv[..., 384:768], qkv[..., 768:]
+        return (lambda: K.attention(q, k, v, 6, 0.125)), 4.0 * nb * 6 * n * n * 64, "flop"
     raise ValueError(kernel)
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", required=True, choices=["preprocess", "resln", "gemm", "deform"])
+    ap.add_argument("--kernel", required=True, choices=["preprocess", "resln", "gemm", "deform", "attn", "attn_win"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)

@@ -184,6 +184,81 @@ class FastBasketballDetector:
         K.check_device_status(self.device)
         return hb.numpy().copy(), hl.numpy().copy()
 
+    def detect_stream(self, batches):
+        """Pipelined detection over a stream of frame batches (a video decoder's output): yields
+        (boxes [N,300,4], logits [N,300,11]) numpy arrays for each uint8 tensor [N, H, W, 3] of `batches`, in order.
+
+        All batches must have one shape; host tensors should be pinned. The host-to-device copy of batch i+1 runs
+        on its own stream while batch i is preprocessed and run on this instance's stream, and the outputs of
+        batch i come back on a third stream (device-to-device into a slot buffer, then to pinned host memory)
+        while batch i+1 computes.
+        Two slots of device frames and outputs alternate; events order every reuse. Results are identical to
+        detect_frames on the same batch."""
+        it = iter(batches)
+        first = next(it, None)
+        if first is None:
+            return
+        if first.dtype != torch.uint8 or first.dim() != 4 or first.shape[-1] != 3:
+            raise ValueError("frames must be a uint8 tensor of shape (N, H, W, 3)")
+        shape = tuple(first.shape)
+        n, h, w, _ = shape
+        with _GPU_LOCK, torch.cuda.device(self.device):
+            runner = self._runner(n)
+            mode, xt, yt = self._taps(w, h)
+            h2d = torch.cuda.Stream(self.device)   # copies in; never waits for compute of earlier batches
+            d2h = torch.cuda.Stream(self.device)   # copies out; waits for each batch's compute
+            dev = [torch.empty(shape, dtype=torch.uint8, device=self.device) for _ in range(2)]
+            out_dev = [(torch.empty_like(runner.boxes), torch.empty_like(runner.logits)) for _ in range(2)]
+            out_host = [(torch.empty(runner.boxes.shape, dtype=torch.float32, pin_memory=True),
+                         torch.empty(runner.logits.shape, dtype=torch.float32, pin_memory=True)) for _ in range(2)]
+            ev = {k: [torch.cuda.Event() for _ in range(2)] for k in ("h2d", "free", "comp", "d2h")}
+        used = [False, False]
+        keep = [None, None]  # host batches stay referenced until their copy has certainly completed
+
+        def enqueue(i: int, frames: torch.Tensor):
+            if tuple(frames.shape) != shape or frames.dtype != torch.uint8:
+                raise ValueError("every batch of a stream must have the first batch's shape and dtype")
+            s = i & 1
+            with _GPU_LOCK, torch.cuda.device(self.device):
+                with torch.cuda.stream(h2d):
+                    if used[s]:
+                        h2d.wait_event(ev["free"][s])           # the slot's previous frames were preprocessed
+                    dev[s].copy_(frames, non_blocking=True)
+                    ev["h2d"][s].record(h2d)
+                    keep[s] = frames
+                with torch.cuda.stream(self.stream):
+                    self.stream.wait_event(ev["h2d"][s])
+                    K.preprocess_batch([(dev[s][k], xt, yt, mode) for k in range(n)], self._lut, INPUT, "patch16",
+                                       out=runner.x)
+                    ev["free"][s].record(self.stream)
+                    boxes, logits = runner.run()
+                    if used[s]:
+                        self.stream.wait_event(ev["d2h"][s])     # the slot's previous outputs reached the host
+                    out_dev[s][0].copy_(boxes)
+                    out_dev[s][1].copy_(logits)
+                    ev["comp"][s].record(self.stream)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(ev["comp"][s])
+                    out_host[s][0].copy_(out_dev[s][0], non_blocking=True)
+                    out_host[s][1].copy_(out_dev[s][1], non_blocking=True)
+                    ev["d2h"][s].record(d2h)
+                used[s] = True
+
+        def collect(i: int):
+            s = i & 1
+            ev["d2h"][s].synchronize()
+            keep[s] = None
+            K.check_device_status(self.device)
+            return out_host[s][0].numpy().copy(), out_host[s][1].numpy().copy()
+
+        enqueue(0, first)
+        i = 0
+        for frames in it:
+            enqueue(i + 1, frames)
+            yield collect(i)
+            i += 1
+        yield collect(i)
+
     def detect_frames(self, frames: torch.Tensor) -> tuple[np.ndarray, np.ndarray]:
         """Frames already in a uint8 tensor [N, H, W, 3] (one size), ideally in pinned host memory (a video
         decoder's output buffer) or on this device. One H2D copy, preprocessing, the captured forward and one

@@ -137,3 +137,17 @@ def test_two_instances_two_threads(det):
     [t.start() for t in th]
     [t.join() for t in th]
     assert not errors
+
+
+def test_detect_stream_matches_detect_frames(det):
+    """The pipelined stream API gives, batch for batch, exactly what detect_frames gives on the same frames —
+    including when batches alternate between two pinned host buffers and the slots are reused."""
+    bufs = [torch.from_numpy(np.stack([frame(40 + 3 * j + i) for i in range(3)])).pin_memory() for j in range(2)]
+    expected = [det.detect_frames(b) for b in bufs]
+    order = [0, 1, 1, 0, 1, 0, 0]
+    got = list(det.detect_stream(bufs[j] for j in order))
+    assert len(got) == len(order)
+    for (gb, gl), j in zip(got, order):
+        assert np.array_equal(gb, expected[j][0]) and np.array_equal(gl, expected[j][1])
+    with pytest.raises(ValueError):
+        list(det.detect_stream([bufs[0], bufs[0][:2]]))

@@ -48,6 +48,7 @@ typedef struct CUstream_st* ko_stream_t; /* identical to cudaStream_t */
 #define KO_ACT_NONE 0
 #define KO_ACT_GELU 1 /* exact erf GELU: 0.5 v (1 + erf(v / sqrt 2)) */
 #define KO_ACT_RELU 2
+#define KO_ACT_SILU 3 /* v / (1 + exp(-v)); ko_layernorm only */
 
 /* --- status / version ------------------------------------------------------------------------------------- */
 
@@ -101,6 +102,20 @@ int ko_preprocess_batch(const ko_image_desc* images, int n, const float* lut, in
 int ko_residual_layernorm(const float* h, const float* o, const float* bias, const float* scale, const float* gamma,
                           const float* beta, float eps, int64_t rows, int64_t C, float* h_out, float* y,
                           ko_stream_t stream);
+
+/* y = act(LayerNorm(x) * gamma + beta) over rows of C (biased variance, eps inside the square root), act
+ * KO_ACT_NONE or KO_ACT_SILU. x, y: float32 [rows][C], C % 4 == 0, C <= 1024; y may alias x. Replaces the plain
+ * mx.fast.layer_norm calls of the model (fast_rfdetr/model.py:80-82) and, with SiLU, the channel LayerNorm + SiLU
+ * of the projector's conv blocks (model.py:157-158). */
+int ko_layernorm(const float* x, const float* gamma, const float* beta, float eps, int64_t rows, int64_t C, int act,
+                 float* y, ko_stream_t stream);
+
+/* cols[(b*H + y)*W + x][tap*C + c] = x[b][y + dy - 1][x + dx - 1][c] (tap = 3*dy + dx, zero outside the image):
+ * the im2col of a 3x3, stride-1, padding-1 convolution on an NHWC float32 tensor, in the column order of a conv
+ * weight [out][3][3][in] flattened to [out][9*in]. C % 4 == 0; x, cols 16-byte aligned. Replaces the padded
+ * mx.conv2d of the projector's 3x3 convolutions (fast_rfdetr/model.py:154-156) as the A operand of
+ * ko_linear_f32_packed. */
+int ko_im2col3x3(const float* x, int64_t B, int64_t H, int64_t W, int64_t C, float* cols, ko_stream_t stream);
 
 /* --- deformable-attention sampling (single level) ----------------------------------------------------------- */
 

@@ -18,7 +18,7 @@ KO_ERR_DEVICE_TIMEOUT = 1003
 
 KO_LAYOUT_HWC, KO_LAYOUT_CHW, KO_LAYOUT_PATCH16 = 0, 1, 2
 KO_RESIZE_REFERENCE, KO_RESIZE_OPENCV = 0, 1
-KO_ACT_NONE, KO_ACT_GELU, KO_ACT_RELU = 0, 1, 2
+KO_ACT_NONE, KO_ACT_GELU, KO_ACT_RELU, KO_ACT_SILU = 0, 1, 2, 3
 
 _i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p
 
@@ -45,6 +45,8 @@ SIGNATURES = {
     "ko_linear_gelu_f32": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
     "ko_linear_gelu_f32_noalloc": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "ko_attention_f32": (_i32, [_vp, _vp, _vp, _vp] + [_i64] * 12 + [_f32, _vp, _vp]),
+    "ko_layernorm": (_i32, [_vp, _vp, _vp, _f32, _i64, _i64, _i32, _vp, _vp]),
+    "ko_im2col3x3": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _vp]),
 }
 
 _lock = threading.Lock()
@@ -78,7 +80,7 @@ def lib() -> ctypes.CDLL:
 # Kernel-launching entry points, counted per call (bench.py reports launches per step from these counts).
 LAUNCHING = {"ko_preprocess": 1, "ko_preprocess_batch": 1, "ko_residual_layernorm": 1, "ko_deform_attn": 1,
              "ko_pack_weight_tf32x3": 1, "ko_linear_f32_packed": 1, "ko_linear_gelu_f32": 2,
-             "ko_linear_gelu_f32_noalloc": 2, "ko_attention_f32": 1}
+             "ko_linear_gelu_f32_noalloc": 2, "ko_attention_f32": 1, "ko_layernorm": 1, "ko_im2col3x3": 1}
 launch_count: dict[str, int] = {}
 
 

@@ -1,4 +1,6 @@
 // Fused residual add + LayerNorm, fp32:  h_out = h + (o + bias) * scale;  y = LN(h_out) * gamma + beta.
+// The same kernel without the residual (ko_layernorm) is the plain LayerNorm of the model's other norms, with an
+// optional SiLU on its output (the projector's conv -> channel LayerNorm -> SiLU blocks, model.py:148-158).
 //
 // Semantics: the reference kernel fast_rfdetr/kernels.py:9-48 (residual_layernorm) and its unfused form
 // model.py:140-141 / 144-145 with mx.fast.layer_norm (biased variance, eps inside the square root).
@@ -13,11 +15,17 @@ namespace {
 
 constexpr int kRowsPerBlock = 8;
 
-template <int V>
+__device__ __forceinline__ float apply_act(float r, int act) {
+  return act == KO_ACT_SILU ? r / (1.0f + expf(-r)) : r;
+}
+
+// RESID: h_out = h + (o + bias) * scale is normalised (and written); otherwise h itself is normalised and h_out is
+// not written (plain LayerNorm). ACT: KO_ACT_NONE or KO_ACT_SILU on the normalised output.
+template <int V, bool RESID>
 __global__ void __launch_bounds__(32 * kRowsPerBlock) residual_ln_kernel(
     const float* h, const float* __restrict__ o, const float* __restrict__ bias, const float* __restrict__ scale,
     const float* __restrict__ gamma, const float* __restrict__ beta, float eps, int64_t rows, int C4,
-    float* h_out, float* __restrict__ y) {
+    float* h_out, float* __restrict__ y, int act) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -29,7 +37,10 @@ __global__ void __launch_bounds__(32 * kRowsPerBlock) residual_ln_kernel(
 #pragma unroll
   for (int i = 0; i < V; ++i) {
     const int c = lane + i * 32;
-    if (c < C4) {
+    if (c < C4 && !RESID) {
+      v[i] = h4[c];
+      sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    } else if (c < C4) {
       const float4 hv = h4[c];
       const float4 ov = __ldg(o4 + c);
       const float4 bv = bias ? __ldg(reinterpret_cast<const float4*>(bias) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -67,12 +78,12 @@ __global__ void __launch_bounds__(32 * kRowsPerBlock) residual_ln_kernel(
     if (c < C4) {
       const float4 g = __ldg(reinterpret_cast<const float4*>(gamma) + c);
       const float4 b = __ldg(reinterpret_cast<const float4*>(beta) + c);
-      ho4[c] = v[i];
+      if (RESID) ho4[c] = v[i];
       float4 r;
-      r.x = (v[i].x - mean) * rstd * g.x + b.x;
-      r.y = (v[i].y - mean) * rstd * g.y + b.y;
-      r.z = (v[i].z - mean) * rstd * g.z + b.z;
-      r.w = (v[i].w - mean) * rstd * g.w + b.w;
+      r.x = apply_act((v[i].x - mean) * rstd * g.x + b.x, act);
+      r.y = apply_act((v[i].y - mean) * rstd * g.y + b.y, act);
+      r.z = apply_act((v[i].z - mean) * rstd * g.z + b.z, act);
+      r.w = apply_act((v[i].w - mean) * rstd * g.w + b.w, act);
       y4[c] = r;
     }
   }
@@ -80,11 +91,32 @@ __global__ void __launch_bounds__(32 * kRowsPerBlock) residual_ln_kernel(
 
 template <int V>
 int launch(const float* h, const float* o, const float* bias, const float* scale, const float* gamma,
-           const float* beta, float eps, int64_t rows, int C4, float* h_out, float* y, cudaStream_t s) {
+           const float* beta, float eps, int64_t rows, int C4, float* h_out, float* y, int act, cudaStream_t s) {
   const int64_t blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
-  residual_ln_kernel<V><<<static_cast<unsigned>(blocks), 32 * kRowsPerBlock, 0, s>>>(h, o, bias, scale, gamma, beta,
-                                                                                   eps, rows, C4, h_out, y);
-  return ko::check_launch("ko_residual_layernorm");
+  if (o)
+    residual_ln_kernel<V, true><<<static_cast<unsigned>(blocks), 32 * kRowsPerBlock, 0, s>>>(
+        h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, act);
+  else
+    residual_ln_kernel<V, false><<<static_cast<unsigned>(blocks), 32 * kRowsPerBlock, 0, s>>>(
+        h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, act);
+  return ko::check_launch(o ? "ko_residual_layernorm" : "ko_layernorm");
+}
+
+int dispatch(const float* h, const float* o, const float* bias, const float* scale, const float* gamma,
+             const float* beta, float eps, int64_t rows, int64_t C, float* h_out, float* y, int act,
+             cudaStream_t s) {
+  const int C4 = static_cast<int>(C / 4);
+  const int V = (C4 + 31) / 32;
+  switch (V) {
+    case 1: return launch<1>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, act, s);
+    case 2: return launch<2>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, act, s);
+    case 3: return launch<3>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, act, s);
+    case 4: return launch<4>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, act, s);
+    case 5: return launch<5>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, act, s);
+    case 6: return launch<6>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, act, s);
+    case 7: return launch<7>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, act, s);
+    default: return launch<8>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, act, s);
+  }
 }
 
 }  // namespace
@@ -102,17 +134,22 @@ extern "C" int ko_residual_layernorm(const float* h, const float* o, const float
     if (p && !ko::aligned16(p)) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_residual_layernorm: pointers must be 16-byte aligned");
   if (rows > (int64_t(1) << 31) * kRowsPerBlock)
     return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_residual_layernorm: too many rows");
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int C4 = static_cast<int>(C / 4);
-  const int V = (C4 + 31) / 32;
-  switch (V) {
-    case 1: return launch<1>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, s);
-    case 2: return launch<2>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, s);
-    case 3: return launch<3>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, s);
-    case 4: return launch<4>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, s);
-    case 5: return launch<5>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, s);
-    case 6: return launch<6>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, s);
-    case 7: return launch<7>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, s);
-    default: return launch<8>(h, o, bias, scale, gamma, beta, eps, rows, C4, h_out, y, s);
-  }
+  return dispatch(h, o, bias, scale, gamma, beta, eps, rows, C, h_out, y, KO_ACT_NONE,
+                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ko_layernorm(const float* x, const float* gamma, const float* beta, float eps, int64_t rows, int64_t C,
+                            int act, float* y, ko_stream_t stream) {
+  if (rows < 0 || C < 4 || C % 4 != 0 || C > 1024)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_layernorm: C must be a multiple of 4 in [4, 1024]");
+  if (act != KO_ACT_NONE && act != KO_ACT_SILU)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_layernorm: act must be KO_ACT_NONE or KO_ACT_SILU");
+  if (rows == 0) return KO_OK;
+  if (!x || !gamma || !beta || !y) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_layernorm: null pointer");
+  const void* ptrs[] = {x, gamma, beta, y};
+  for (const void* p : ptrs)
+    if (!ko::aligned16(p)) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_layernorm: pointers must be 16-byte aligned");
+  if (rows > (int64_t(1) << 31) * kRowsPerBlock) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_layernorm: too many rows");
+  return dispatch(x, nullptr, nullptr, nullptr, gamma, beta, eps, rows, C, nullptr, y, act,
+                  reinterpret_cast<cudaStream_t>(stream));
 }

@@ -99,6 +99,37 @@ def residual_layernorm(h, o, bias, scale, gamma, beta, eps):
     return h_out, y
 
 
+def layernorm(x, gamma, beta, eps, act=None, out=None):
+    """act(LayerNorm(x) * gamma + beta) over the last dimension (C % 4 == 0, C <= 1024), act None or 'silu'.
+    The plain mx.fast.layer_norm of the reference (model.py:80-82); with 'silu', the projector's channel
+    LayerNorm + SiLU (model.py:157-158) in one pass."""
+    _need(x, "x")
+    c = x.shape[-1]
+    for name, t in (("gamma", gamma), ("beta", beta)):
+        if _need(t, name).numel() != c:
+            raise ValueError(f"{name} must have {c} elements")
+    if act not in (None, "none", "silu"):
+        raise ValueError("act must be None or 'silu'")
+    if out is None:
+        out = torch.empty_like(x)
+    call("ko_layernorm", x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), float(eps), x.numel() // c if c else 0, c,
+         _lib.KO_ACT_SILU if act == "silu" else _lib.KO_ACT_NONE, out.data_ptr(), _stream())
+    return out
+
+
+def im2col3x3(x, out=None):
+    """x: float32 NHWC [B, H, W, C] -> [B*H*W, 9*C], the im2col of a 3x3 / stride 1 / padding 1 convolution in the
+    column order of a [out][3][3][in] weight (the projector's mx.conv2d, model.py:154-156, as a GEMM operand)."""
+    _need(x, "x")
+    if x.dim() != 4:
+        raise ValueError("x must be [B, H, W, C]")
+    b, h, w, c = x.shape
+    if out is None:
+        out = torch.empty((b * h * w, 9 * c), dtype=torch.float32, device=x.device)
+    call("ko_im2col3x3", x.data_ptr(), b, h, w, c, out.data_ptr(), _stream())
+    return out
+
+
 def residual_layernorm_into(h, o, bias, scale, gamma, beta, eps, h_out, y):
     """In-place variant for preallocated buffers (h_out may be h). No shape checks beyond the C ABI's."""
     c = h.shape[-1]

@@ -155,9 +155,9 @@ class RFDETR:
 
     # ---- backbone -----------------------------------------------------------------------------------------
     @staticmethod
-    def _ln_op(x, ln):
+    def _ln_op(x, ln, act=None):
         w, b, eps = ln
-        return F.layer_norm(x, (x.shape[-1],), w, b, eps)
+        return K.layernorm(x.contiguous(), w, b, eps, act)
 
     def backbone(self, patches: torch.Tensor):
         """patches [B, 1600, 768] -> four feature maps [B, 40, 40, C] (model.py:84-105, fused path)."""
@@ -195,12 +195,9 @@ class RFDETR:
         if cv["k"] == 1:
             cols = x.reshape(b * hh * ww, cin)
         else:
-            xp = F.pad(x, (0, 0, 1, 1, 1, 1))
-            cols = torch.cat([xp[:, dy:dy + hh, dx:dx + ww] for dy in range(3) for dx in range(3)], -1)
-            cols = cols.reshape(b * hh * ww, 9 * cin)
+            cols = K.im2col3x3(x.contiguous())                                                   # [B*H*W, 9*cin]
         y = cv["dense"](cols)
-        y = self._ln_op(y, cv["ln"])
-        return F.silu(y).reshape(b, hh, ww, -1)
+        return self._ln_op(y, cv["ln"], "silu").reshape(b, hh, ww, -1)
 
     def projector(self, feats):
         y = self._convx(torch.cat(feats, -1), self.cv1)

@@ -170,6 +170,32 @@ def test_residual_layernorm_widths(cuda, c):
     assert_close(y, ry)
 
 
+@pytest.mark.parametrize("c", [128, 256, 384])
+@pytest.mark.parametrize("act", [None, "silu"])
+def test_layernorm_plain_and_silu(cuda, c, act):
+    """ko_layernorm: the residual kernel without the residual, optionally with SiLU on its output."""
+    r = np.random.default_rng(c + (act is not None))
+    x = (3 * r.standard_normal((1000, c)) + 0.5).astype(np.float32)
+    g = (1 + 0.1 * r.standard_normal(c)).astype(np.float32)
+    b = (0.1 * r.standard_normal(c)).astype(np.float32)
+    _, ref = OK.residual_layernorm(x, np.zeros_like(x), None, None, g, b, 1e-5)
+    if act == "silu":
+        ref = ref / (1 + np.exp(-ref))
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    assert_close(K.layernorm(t(x), t(g), t(b), 1e-5, act), ref, what=f"layernorm c={c} act={act}")
+
+
+@pytest.mark.parametrize("shape", [(2, 7, 9, 12), (4, 40, 40, 128)])
+def test_im2col3x3_matches_padded_shifts(cuda, shape):
+    """ko_im2col3x3 is a pure copy: bit-exact against the padded nine-view concatenation."""
+    x = torch.randn(*shape, generator=torch.Generator().manual_seed(shape[-1]))
+    b, h, w, c = shape
+    xp = torch.nn.functional.pad(x, (0, 0, 1, 1, 1, 1))
+    ref = torch.cat([xp[:, dy:dy + h, dx:dx + w] for dy in range(3) for dx in range(3)], -1).reshape(b * h * w, 9 * c)
+    got = K.im2col3x3(x.to(cuda)).cpu()
+    assert torch.equal(got, ref)
+
+
 # ---------------------------------------------------------------- deformable sampling
 def deform_inputs(r, b, row=256, nq=300, nh=16, npts=2):
     value = r.standard_normal((b, 1600, row)).astype(np.float32)

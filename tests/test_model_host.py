@@ -50,6 +50,17 @@ def _attention(q, k, v, heads, scale, out=None):
     return (p @ vh).transpose(1, 2).reshape(b, n, w)
 
 
+def _layernorm(x, g, b, eps, act=None, out=None):
+    y = F.layer_norm(x, (x.shape[-1],), g, b, eps)
+    return F.silu(y) if act == "silu" else y
+
+
+def _im2col3x3(x, out=None):
+    b, h, w, c = x.shape
+    xp = F.pad(x, (0, 0, 1, 1, 1, 1))
+    return torch.cat([xp[:, dy:dy + h, dx:dx + w] for dy in range(3) for dx in range(3)], -1).reshape(b * h * w, 9 * c)
+
+
 @pytest.fixture()
 def cpu_model(monkeypatch):
     import kernelopt_b200.kernels as K
@@ -59,6 +70,8 @@ def cpu_model(monkeypatch):
     monkeypatch.setattr(K, "residual_layernorm", _rln)
     monkeypatch.setattr(K, "deform_attn", _deform)
     monkeypatch.setattr(K, "attention", _attention)
+    monkeypatch.setattr(K, "layernorm", _layernorm)
+    monkeypatch.setattr(K, "im2col3x3", _im2col3x3)
     monkeypatch.setattr(K, "status_word", lambda *a: None)
     w = random_weights(0)
 

@@ -3,7 +3,8 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N
 
-A step (ours) is one pass of the whole path over B seeded 1920x1080 uint8 frames per GPU: the preprocessing
+A step (ours) is one pass of the whole path over B (default 64) seeded 1920x1080 uint8 frames per GPU — the
+512-frame stream of the full-forward config split over 8 GPUs, one step per GPU: the preprocessing
 kernel (bit-exact cv2 resize + normalise, written straight into the patch-embedding layout) and the captured
 fp32 forward (backbone, projector, top-300 selection, decoder, heads). Frames are independent, so N GPUs each
 take their own B frames (weak scaling, no collective on the data path); time is the max over ranks of the
@@ -34,11 +35,12 @@ WORKLOAD = ("RF-DETR-Medium fp32 inference on seeded 1920x1080 uint8 BGR frames:
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per GEMM launch, mean over the 95 GEMM launches of
-# one step, from one ncu capture of this benchmark at 16 frames per step:
+# one step, from one ncu capture of this benchmark at each batch size:
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --cache-control none
-#       --clock-control none -k regex:gemm_tf32x3 -c 95 python bench.py --batch 16 --steps 1 --warmup 3
-# (9258 MB over the 95 launches; the algorithmic bytes of the same launches are 9905 MB).
-GEMM_TRAFFIC_PER_LAUNCH = {16: 97.45e6}
+#       --clock-control none -k regex:gemm_tf32x3 -c 95 python bench.py --batch B --steps 1 --warmup 3
+# 64 frames: 38 876 MB over the 95 launches (algorithmic bytes of the same launches: 38 916 MB);
+# 16 frames: 9 258 MB (algorithmic 9 905 MB).
+GEMM_TRAFFIC_PER_LAUNCH = {64: 409.2e6, 16: 97.45e6}
 
 
 def frames_for(rank: int, n: int) -> np.ndarray:
@@ -239,6 +241,24 @@ def run_ours(args, rank: int, world: int):
     e2e = world * B * args.steps / e2e_secs
     barrier()
 
+    # ---- latency of one batch of 1 and of 3 frames (config 5's latency runs), frames on the device ----
+    latency = {}
+    for nb in (1, 3):
+        r_nb = det._runner(nb)
+        items_nb = items[:nb]
+        ts = []
+        with torch.cuda.stream(stream):
+            for it in range(25):
+                l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                l0.record(stream)
+                K.preprocess_batch(items_nb, det._lut, 640, "patch16", out=r_nb.x)
+                r_nb.run()
+                l1.record(stream)
+                l1.synchronize()
+                if it >= 5:
+                    ts.append(l0.elapsed_time(l1))
+        latency[f"frames_{nb}"] = statistics.median(ts)
+
     # ---- per-kernel timing (CUDA events around each launch, eager) and launch count ----
     per, launches_per_step = instrumented_step(det, runner.x, items, K)
     peaks = measured_peaks()
@@ -276,7 +296,9 @@ def run_ours(args, rank: int, world: int):
                     "path": "FastBasketballDetector.detect_stream(pinned uint8 frame batches) -> numpy, "
                             "H2D / D2H on a copy stream overlapping the neighbouring steps' compute"},
             "gpu_launches": int(launches_per_step * args.steps),
-            "roofline": roofline, "kernels": kernels, "clocks": clk.summary()}
+            "roofline": roofline, "kernels": kernels, "clocks": clk.summary(),
+            "latency_ms": dict(latency, note="median CUDA-event time of preprocessing + forward for one batch, "
+                                             "frames resident on the device")}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         fps, n, cores = cpu_reference_run(10_000, budget_s=args.cpu_seconds)
         line["cpu_baseline"] = {"value": fps, "unit": "frames/s", "cores": cores, "kind": "port",
@@ -294,7 +316,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--batch", type=int, default=16, help="frames per step per GPU")
+    ap.add_argument("--batch", type=int, default=64,
+                    help="frames per step per GPU (64: config 5's 512-frame stream over 8 GPUs)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")

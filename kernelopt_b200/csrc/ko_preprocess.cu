@@ -8,8 +8,8 @@
 // B200 design: every thread produces 4 consecutive outputs and writes them with one 128-bit store, from source
 // rows staged in shared memory with 16-byte copies, so both the row reads and the output writes are fully
 // coalesced. Outputs up to 682 wide (the model's 640) use the band kernel: one CTA per band of output rows, with
-// the x taps in registers, the LUT in shared memory and the next row pair prefetched with cp.async while the
-// current one is computed. Wider outputs use one CTA per output row. All images of a batch (any sizes) go in one
+// the x taps in registers, the LUT in shared memory and the next row pair prefetched with cp.async into a ring of
+// three buffers while the current one is computed. Wider outputs use one CTA per output row. All images of a batch (any sizes) go in one
 // launch. Three output layouts share the kernel: HWC (the reference's), CHW (NCHW batches) and PATCH16 (the
 // im2col of the ViT 16x16 patch embedding, which turns that convolution into a plain GEMM).
 #include <cstring>
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(const __grid_const
 // Everything that does not depend on the row is set up once per CTA and kept on chip: each thread's x taps (the
 // clamped xtab entries of its 4 output elements), their RGB channels and output column offset live in registers, the
 // 768-entry LUT in shared memory. The two source rows of output row y+1 are fetched with cp.async (16-byte,
-// L2-only) into the other half of a double buffer while row y is computed, so the HBM reads of the next row
+// L2-only) into the next buffer of a ring of three while row y is computed, so the HBM reads of the next row
 // overlap the arithmetic of this one. Per output element the loop does 4 byte loads from shared memory, the
 // integer tap arithmetic, one LUT load from shared memory and a quarter of a 128-bit store.
 // ---------------------------------------------------------------------------------------------------------
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(kBandThreads) preprocess_band_kernel(const __g
                                                                        int row_cap, int band) {
   extern __shared__ __align__(16) uint8_t smem[];
   float* slut = reinterpret_cast<float*>(smem);  // [3][256]
-  uint8_t* rowbuf = smem + 768 * 4;              // [2 buffers][2 rows][row_cap]
+  uint8_t* rowbuf = smem + 768 * 4;              // [3 buffers][2 rows][row_cap]
   const ImageParams& im = p.img[blockIdx.y];
   const int tid = threadIdx.x;
   const int y_begin = blockIdx.x * band;
@@ -268,11 +268,12 @@ __global__ void __launch_bounds__(kBandThreads) preprocess_band_kernel(const __g
     obase[k] = out + img_base + col_off;
   }
 
-  for (int y = y_begin; y < y_end; ++y) {
-    const int buf = (y - y_begin) & 1;
+  // Three row-pair buffers: the pair of row y+1 is staged into the buffer row y-2 used, which every thread has
+  // finished reading before it passed the barrier of row y-1; so one barrier per row suffices.
+  for (int y = y_begin, buf = 0; y < y_end; ++y, buf = buf == 2 ? 0 : buf + 1) {
     const int4 yt = yt_next;
     if (y + 1 < y_end) {
-      yt_next = stage(y + 1, buf ^ 1);
+      yt_next = stage(y + 1, buf == 2 ? 0 : buf + 1);
     } else {
       cp_async_commit();  // empty group keeps the wait count uniform
     }
@@ -288,7 +289,6 @@ __global__ void __launch_bounds__(kBandThreads) preprocess_band_kernel(const __g
                                  : item_values<1>(s0, s1, tap[k], chans[k], yt, slut);
       *reinterpret_cast<float4*>(obase[k] + rt) = v;
     }
-    __syncthreads();  // buffer `buf` is restaged two rows from now
   }
 }
 
@@ -340,7 +340,7 @@ extern "C" int ko_preprocess_batch(const ko_image_desc* images, int n, const flo
     const int64_t target = 8 * static_cast<int64_t>(info.sm_count);
     int band = 16;
     while (band > 1 && n * ((dst + band - 1) / band) < target) band /= 2;
-    const int64_t smem = 768 * 4 + 4 * row_cap;
+    const int64_t smem = 768 * 4 + 6 * row_cap;
     if (smem > info.max_smem_optin) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_preprocess: source rows too wide");
     dim3 grid(static_cast<unsigned>((dst + band - 1) / band), static_cast<unsigned>(n));
     auto kern = n_items <= kBandThreads ? preprocess_band_kernel<1> : preprocess_band_kernel<2>;

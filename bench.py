@@ -125,12 +125,16 @@ def instrumented_step(det, runner_x, items, K):
     from kernelopt_b200 import _lib
     from kernelopt_b200.benchutil import EventTimer, hold_stream
 
-    timers = {n: EventTimer() for n in ("gemm_tf32x3", "attention_tf32x3", "residual_layernorm", "deform_attn",
-                                         "preprocess")}
-    orig = {n: getattr(K, n) for n in ("linear", "attention", "residual_layernorm", "deform_attn", "preprocess_batch")}
+    timers = {n: EventTimer() for n in ("gemm_tf32x3", "gemm_residual_ln", "attention_tf32x3", "residual_layernorm",
+                                         "deform_attn", "preprocess")}
+    orig = {n: getattr(K, n) for n in ("linear", "linear_residual_layernorm", "attention", "residual_layernorm",
+                                       "deform_attn", "preprocess_batch")}
 
     def gemm_work(x, pw, act=None, out=None):
         return 2.0 * (x.numel() // pw.k) * pw.k * pw.n
+
+    def gemm_ln_work(x, pw, *a, **k):
+        return 2.0 * (x.numel() // pw.k) * pw.k * pw.n   # the GEMM's flops; the epilogue is memory work
 
     def attn_work(q, k, v, heads, scale, out=None):
         b, n, w = q.shape
@@ -148,6 +152,7 @@ def instrumented_step(det, runner_x, items, K):
         return float(sum(img.numel() for img, *_ in items_) + len(items_) * dst * dst * 3 * 4)
 
     K.linear = timers["gemm_tf32x3"].wrap(orig["linear"], gemm_work)
+    K.linear_residual_layernorm = timers["gemm_residual_ln"].wrap(orig["linear_residual_layernorm"], gemm_ln_work)
     K.attention = timers["attention_tf32x3"].wrap(orig["attention"], attn_work)
     K.residual_layernorm = timers["residual_layernorm"].wrap(orig["residual_layernorm"], ln_work)
     K.deform_attn = timers["deform_attn"].wrap(orig["deform_attn"], deform_work)
@@ -166,7 +171,7 @@ def instrumented_step(det, runner_x, items, K):
     out = {}
     for n, t in timers.items():
         secs, work, cnt = t.total()
-        out[n] = (secs, work, cnt, "flop" if n in ("gemm_tf32x3", "attention_tf32x3") else "byte")
+        out[n] = (secs, work, cnt, "flop" if n in ("gemm_tf32x3", "gemm_residual_ln", "attention_tf32x3") else "byte")
     return out, launches
 
 

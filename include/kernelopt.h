@@ -144,6 +144,21 @@ int ko_pack_weight_tf32x3(const float* w, int64_t K, int64_t N, float* w_packed,
 int ko_linear_f32_packed(const float* x, const float* w_packed, const float* bias, int64_t M, int64_t K, int64_t N,
                          int act, float* out, int* dev_status, ko_stream_t stream);
 
+/* GEMM with the residual add and LayerNorm in its epilogue, whole rows at a time:
+ *   v = resid + (x @ W + bias) * scale;   y = act((v - mean(v)) / sqrt(var(v) + eps) * gamma + beta)
+ * with the mean and biased variance over the N columns of each row. x float32 [M][K]; W pre-split by
+ * ko_pack_weight_tf32x3; bias, scale, gamma, beta float32 [N] (bias NULL = 0, scale NULL = 1); resid float32
+ * [M][N] or NULL (no residual); h_out float32 [M][N] receives v, or NULL (not written); h_out may alias resid,
+ * y must alias none of x, resid, h_out. act KO_ACT_NONE or KO_ACT_SILU. N one of 128, 192, 256, 384, 512 (a
+ * row spans one CTA, or a cluster of two that exchange row statistics); K % 4 == 0; 16-byte aligned pointers.
+ * The GEMM is the 3xTF32 product of ko_linear_f32_packed. Fuses the reference's next step: its attention
+ * out-projection and fc2 GEMMs followed by residual_layernorm (fast_rfdetr/model.py:121-123, 129-132,
+ * kernels.py:9-67), and also GEMM + LayerNorm + SiLU (model.py:148-158) and GEMM + LayerNorm (model.py:178). */
+int ko_linear_residual_ln_f32_packed(const float* x, const float* w_packed, const float* bias, const float* scale,
+                                     const float* resid, const float* gamma, const float* beta, float eps,
+                                     int64_t M, int64_t K, int64_t N, int act, float* h_out, float* y,
+                                     int* dev_status, ko_stream_t stream);
+
 /* out = GELU_erf(x @ w + bias): packs w into `workspace` (ko_linear_workspace_bytes(K, N) bytes, 16-byte
  * aligned) and runs ko_linear_f32_packed. Replaces linear_gelu_f32 (fast_rfdetr/kernels.py:271-285; kernel
  * source :188-266). */

@@ -25,7 +25,9 @@
 //               into hi / lo and written into shared memory in the MMA's 128-byte-swizzled K-major layout. v is
 //               written transposed (head dim x keys), the K-major form of the P.V product's B operand.
 // Tensor memory (512 columns): two S / P_hi buffers [0,256), P_lo [256,384), two O_j buffers of HD columns from
-// 384. With two S buffers the tensor cores compute S_{j+1} while the softmax warps work on block j.
+// 384. With two S buffers the tensor cores compute S_{j+1} while the softmax warps work on block j, and P_j.V_j
+// issues its P_lo products first and then frees the one P_lo buffer, so the softmax warps write P_{j+1} while
+// the P_hi products of block j run (the softmax of one block overlaps the tensor-core work of the previous).
 // Every wait on an mbarrier is bounded (2 s); on timeout the CTA stops, drains its MMAs, frees tensor memory and
 // reports KO_ERR_DEVICE_TIMEOUT through dev_status.
 #include <algorithm>
@@ -99,8 +101,8 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void split_tf32(float v, float& hi, float& lo) {
-  hi = __uint_as_float(f32_to_tf32_rna(v));
-  lo = __uint_as_float(f32_to_tf32_rna(v - hi));
+  hi = __uint_as_float(f32_to_tf32_rna_int(v));
+  lo = __uint_as_float(f32_to_tf32_rna_int(v - hi));
 }
 
 // 32 lanes x 16 consecutive 32-bit columns, load and store.
@@ -159,7 +161,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
   uint64_t* o_full = bars + 8;    // O_j complete, x2        (1 commit)
   uint64_t* o_empty = bars + 10;  // O_j consumed, x2        (4 softmax warps)
   uint64_t* mma_done = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* plo_free = bars + 13;  // P_j.V_j's P_lo products done (1 commit)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -179,6 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
       mbar_init(&o_empty[i], 4);
     }
     mbar_init(mma_done, 1);
+    mbar_init(plo_free, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -195,7 +199,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
     // ---------------- MMA issuer ----------------
     // Order on the tensor pipe: S_0, then per block j: S_{j+1} (into the other S buffer, overlapping softmax_j),
     // P_j.V_j. S_{j+1} reuses the buffer of P_{j-1}, so it waits for P_{j-1}.V_{j-1} to complete.
-    if (lane == 0) {
+    // The whole warp runs this loop with the same values in every lane; one elected lane issues each MMA.
+    {
       // Descriptors are built once; an MMA's operand is its tile's descriptor plus the byte offset / 16 (the
       // start-address field; shared addresses stay below 2^18 bytes, so the field cannot overflow).
       const uint32_t sb = smem_addr(smem);
@@ -209,57 +214,65 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
       auto issue_s = [&](int j) {  // S_j = Q K_j^T into S buffer j & 1
         const uint32_t d = tmem + kColS + static_cast<uint32_t>(j & 1) * BKEY;
         const uint32_t idesc_s = idesc_tf32(BQ, (keys_of(j) + 15) & ~15);
-#pragma unroll 1
+#pragma unroll
         for (int s = 0; s < C::kKB * 4; ++s) {  // 8-wide k-steps over the head dimension
           const uint64_t off = static_cast<uint64_t>(((s >> 2) * (BQ * 128) + (s & 3) * 32) >> 4);
-          mma_tf32(d, dq_lo + off, dk_hi + off, idesc_s, s == 0 ? 0u : 1u);
-          mma_tf32(d, dq_hi + off, dk_lo + off, idesc_s, 1u);
-          mma_tf32(d, dq_hi + off, dk_hi + off, idesc_s, 1u);
+          mma_tf32_w(d, dq_lo + off, dk_hi + off, idesc_s, s == 0 ? 0u : 1u);
+          mma_tf32_w(d, dq_hi + off, dk_lo + off, idesc_s, 1u);
+          mma_tf32_w(d, dq_hi + off, dk_hi + off, idesc_s, 1u);
         }
-        mma_commit(&s_full[j & 1]);
-        mma_commit(k_empty);
+        mma_commit_w(&s_full[j & 1]);
+        mma_commit_w(k_empty);
       };
-      bool ok = mbar_wait(q_ready, 0, abort_flag) && mbar_wait(k_full, 0, abort_flag);
+      bool ok = warp_wait(q_ready, 0, abort_flag) && warp_wait(k_full, 0, abort_flag);
       if (ok) {
         tc_fence_after();
         issue_s(0);
       }
       for (int j = 0; j < nkb && ok; ++j) {
         if (j + 1 < nkb) {
-          if (!mbar_wait(k_full, static_cast<uint32_t>(j + 1) & 1u, abort_flag)) break;
-          if (j >= 1 && !mbar_wait(&o_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag)) break;
+          if (!warp_wait(k_full, static_cast<uint32_t>(j + 1) & 1u, abort_flag)) break;
+          if (j >= 1 && !warp_wait(&o_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag)) break;
           tc_fence_after();
           issue_s(j + 1);
         }
         // O_j = P_j V_j into O buffer j & 1, once P_j is written, V_j landed and the buffer was consumed
-        if (!mbar_wait(p_full, static_cast<uint32_t>(j) & 1u, abort_flag) ||
-            !mbar_wait(v_full, static_cast<uint32_t>(j) & 1u, abort_flag) ||
-            !mbar_wait(&o_empty[j & 1], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, abort_flag))
+        if (!warp_wait(p_full, static_cast<uint32_t>(j) & 1u, abort_flag) ||
+            !warp_wait(v_full, static_cast<uint32_t>(j) & 1u, abort_flag) ||
+            !warp_wait(&o_empty[j & 1], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, abort_flag))
           break;
         tc_fence_after();
         const uint32_t d = tmem + kColO + static_cast<uint32_t>(j & 1) * HD;
         const uint32_t p_hi = tmem + kColS + static_cast<uint32_t>(j & 1) * BKEY;
         const int ksteps = (keys_of(j) + 7) >> 3;
+        // The P_lo products first, then a commit that hands the P_lo columns back to the softmax warps: they
+        // write P_{j+1} while the P_hi products of this block (two thirds of its MMAs) still run.
 #pragma unroll 1
         for (int kk = 0; kk < ksteps; ++kk) {  // 8 keys per k-step
           const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
-          const uint32_t phi = p_hi + 8 * kk, plo = tmem + kColPlo + 8 * kk;
-          mma_tf32_ts(d, plo, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
-          mma_tf32_ts(d, phi, dv_lo + off, idesc_o, 1u);
-          mma_tf32_ts(d, phi, dv_hi + off, idesc_o, 1u);
+          mma_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
         }
-        mma_commit(&o_full[j & 1]);
-        mma_commit(v_empty);
+        mma_commit_w(plo_free);
+#pragma unroll 1
+        for (int kk = 0; kk < ksteps; ++kk) {
+          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
+          const uint32_t phi = p_hi + 8 * kk;
+          mma_tf32_ts_w(d, phi, dv_lo + off, idesc_o, 1u);
+          mma_tf32_ts_w(d, phi, dv_hi + off, idesc_o, 1u);
+        }
+        mma_commit_w(&o_full[j & 1]);
+        mma_commit_w(v_empty);
       }
-      // Drain: every MMA this thread issued completes before tensor memory is released.
-      mma_commit(mma_done);
+      // Drain: every MMA this warp issued completes before tensor memory is released.
+      mma_commit_w(mma_done);
       volatile int never = 0;
-      if (!mbar_wait(mma_done, 0, &never)) *abort_flag = 1;
+      if (!warp_wait(mma_done, 0, &never)) *abort_flag = 1;
     }
   } else if (warp < kLoadWarp0) {
     // ---------------- softmax + output, one thread per query row ----------------
-    // Block j: max of S_j (pass 1); then, once P_{j-1}.V_{j-1} is complete, O += that block's product (which
-    // also frees the P_lo columns); then P_j = exp2(S_j * c - m) as hi / lo into tensor memory (pass 2).
+    // Block j: max of S_j (pass 1); then, once P_{j-1}.V_{j-1}'s P_lo products are done (the P_lo columns are
+    // free), P_j = exp2(S_j * c - m) as hi / lo into tensor memory (pass 2); then, once all of P_{j-1}.V_{j-1} is
+    // complete, o = o * alpha + that block's product.
     const int quad = warp & 3;  // tensor-memory lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
@@ -306,9 +319,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
       }
       const float m_new = fmaxf(m, mb * a.scale_log2);
       const float alpha = fast_exp2(m - m_new);
-      if (j >= 1 && !add_block(j - 1, alpha_prev)) {
-        ok = false;
-        break;
+      if (j >= 1) {
+        if (!warp_wait(plo_free, static_cast<uint32_t>(j - 1) & 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
       }
       float ls = 0.f;
 #pragma unroll 1
@@ -331,10 +347,14 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
       tmem_st_wait();
       l = l * alpha + ls;
       m = m_new;
-      alpha_prev = alpha;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
+      if (j >= 1 && !add_block(j - 1, alpha_prev)) {
+        ok = false;
+        break;
+      }
+      alpha_prev = alpha;
     }
     if (ok && !add_block(nkb - 1, alpha_prev)) ok = false;
     const int qi = q0 + row;

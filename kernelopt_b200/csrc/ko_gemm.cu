@@ -23,6 +23,7 @@
 // Every wait on an mbarrier is bounded (2 s); on timeout the CTA stops, drains what it issued, frees TMEM and
 // reports KO_ERR_DEVICE_TIMEOUT through dev_status.
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 
@@ -45,13 +46,27 @@ constexpr size_t kSmemBudget = 224 * 1024 - kStoreBytes;  // stage buffers; stag
 // accumulator in the epilogue. The tensor core's fp32 accumulation drops low-order bits at every MMA; with a
 // single accumulator the 2 x K/8 correction MMAs land on a large running sum, which makes the error grow with
 // K. With SPLIT they land on a small one, and the large sum sees only K/8 additions.
-template <int BN, int BKB, bool SPLIT>
+// Epilogue kinds. EPI_ACT: out = act(acc + bias). EPI_LN: v = resid + (acc + bias) * scale over whole rows
+// (the N columns of a row are split over the CTAs of a cluster), y = act(LayerNorm(v) * gamma + beta).
+constexpr int EPI_ACT = 0;
+constexpr int EPI_LN = 1;
+
+// Row statistics exchange of the LayerNorm epilogue: per tile parity, the two epilogue warps of a lane
+// quadrant publish (mean, M2) of their half of the row [2][2][128] float2, and the cluster peer's CTA-level
+// (mean, M2) lands in [2][128] float2; two mbarriers count the peer's arrivals, four (one per lane quadrant)
+// the two warps of a pair, and eight (one per epilogue warp) the TMA loads into the warps' staging tiles.
+constexpr uint32_t kLnStatBytes = 2 * 2 * 128 * 8 + 2 * 128 * 8 + 2 * 8 + 4 * 8 + 8 * 8;
+constexpr uint32_t kLnStatRegion = 6400;
+static_assert(kLnStatBytes <= kLnStatRegion, "stat region");
+
+template <int BN, int BKB, bool SPLIT, int EPI = EPI_ACT>
 struct Cfg {
   static constexpr int kBK = BKB / 4;                       // fp32 elements per k-block
   static constexpr uint32_t kATileBytes = BM * BKB;
   static constexpr uint32_t kBTileBytes = BN * BKB;
   static constexpr uint32_t kStageBytes = 2 * kATileBytes + 2 * kBTileBytes;
-  static constexpr int kStagesRaw = static_cast<int>(kSmemBudget / kStageBytes);
+  static constexpr uint32_t kStatBytes = EPI == EPI_LN ? kLnStatRegion : 0;
+  static constexpr int kStagesRaw = static_cast<int>((kSmemBudget - kStatBytes) / kStageBytes);
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr uint32_t kAccCols = BN * (SPLIT ? 2 : 1);  // TMEM columns of one tile's accumulator(s)
   static constexpr int kAccBufs = (2 * kAccCols <= 512) ? 2 : 1;
@@ -59,7 +74,7 @@ struct Cfg {
   static constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
                                         : kTmemNeed <= 256 ? 256 : 512;
   static constexpr uint32_t kTxBytes = kATileBytes + 2 * kBTileBytes;
-  static constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + kStoreBytes + 256;
+  static constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + kStoreBytes + 256 + kStatBytes;
   static constexpr uint32_t kSbo = 8 * BKB;                 // bytes between 8-row groups
   static constexpr uint32_t kLayout = BKB == 128 ? 2u : 4u;  // descriptor layout: 128B / 64B swizzle
   static_assert(kStages >= 2, "stage does not fit");
@@ -72,6 +87,38 @@ struct GemmArgs {
   int* dev_status;
   int M, N, K, act;
   int m_tiles, n_tiles, k_blocks;
+  // EPI_LN only
+  const float* scale;  // per-column multiplier of (acc + bias), or null (1)
+  const float* resid;  // residual added before the LayerNorm [M][N], or null
+  const float* gamma;
+  const float* beta;
+  float eps;
+  int write_v;  // store v = resid + (acc + bias) * scale through map_v
+  int cs;       // CTAs per cluster = N / BN
+};
+
+// Tiles of one CTA. EPI_ACT: tile t of the m_tiles x n_tiles grid, CTAs strided over tiles. EPI_LN: tile t is
+// row block t; the cs CTAs of a cluster take the same row block, CTA rank r the columns [r*BN, (r+1)*BN).
+template <int EPI>
+struct TileSched {
+  int first, step, count, n_tiles, col0;
+  __device__ explicit TileSched(const GemmArgs& a, int bn) {
+    if (EPI == EPI_LN) {
+      first = a.cs > 1 ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+      step = a.cs > 1 ? static_cast<int>(cluster_count_x()) : static_cast<int>(gridDim.x);
+      count = a.m_tiles;
+      n_tiles = 1;
+      col0 = (a.cs > 1 ? static_cast<int>(cluster_ctarank()) : 0) * bn;
+    } else {
+      first = blockIdx.x;
+      step = gridDim.x;
+      count = a.m_tiles * a.n_tiles;
+      n_tiles = a.n_tiles;
+      col0 = 0;
+    }
+  }
+  __device__ int m0(int tile) const { return (tile / n_tiles) * BM; }
+  __device__ int n0(int tile, int bn) const { return (tile % n_tiles) * bn + col0; }
 };
 
 __device__ __forceinline__ float apply_act(float v, int act) {
@@ -88,12 +135,37 @@ __device__ __forceinline__ uint64_t desc_k(uint32_t addr) {
          (static_cast<uint64_t>(kLayout) << 61);
 }
 
-template <int BN, int BKB, bool SPLIT>
+// TMEM store of 32 lanes x 32 consecutive columns (the inverse of tmem_ld_32x32b_x32).
+__device__ __forceinline__ void tmem_store_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_store_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// (mean, M2) of two equal-sized groups of n values each, combined in the order (a, b) (Chan et al., 1979).
+__device__ __forceinline__ float2 combine_stats(float2 a, float2 b, float n) {
+  const float d = b.x - a.x;
+  return make_float2(a.x + 0.5f * d, a.y + b.y + d * d * (0.5f * n));
+}
+
+__device__ __forceinline__ float ln_act(float r, int act) {
+  return act == KO_ACT_SILU ? r / (1.0f + expf(-r)) : r;
+}
+
+template <int BN, int BKB, bool SPLIT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_whi,
                        const __grid_constant__ CUtensorMap map_wlo, const __grid_constant__ CUtensorMap map_out,
+                       const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_r,
                        const GemmArgs args) {
-  using C = Cfg<BN, BKB, SPLIT>;
+  using C = Cfg<BN, BKB, SPLIT, EPI>;
   constexpr int S = C::kStages;
   constexpr int NB = C::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
@@ -109,9 +181,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* mma_done = acc_empty + 2;  // teardown drain        (1 commit)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // EPI_LN: row statistics (see kLnStatBytes)
+  float2* pair_stats = reinterpret_cast<float2*>(store_smem + kStoreBytes + 256);
+  float2* peer_stats = pair_stats + 2 * 2 * 128;
+  uint64_t* peer_bar = reinterpret_cast<uint64_t*>(peer_stats + 2 * 128);
+  uint64_t* pair_bar = peer_bar + 2;
+  uint64_t* load_bar = pair_bar + 4;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_tiles = args.m_tiles * args.n_tiles;
+  const TileSched<EPI> ts(args, BN);
+  const int num_tiles = ts.count;
+  const bool clustered = EPI == EPI_LN && args.cs > 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -124,12 +204,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[a], 8);
     }
     mbar_init(mma_done, 1);
+    if (EPI == EPI_LN) {
+      mbar_init(&peer_bar[0], 128);  // one arrival per lane of the peer's four first-half epilogue warps
+      mbar_init(&peer_bar[1], 128);
+      for (int q = 0; q < 4; ++q) mbar_init(&pair_bar[q], 64);  // every thread of the two warps of a quadrant
+      for (int w = 0; w < 8; ++w) mbar_init(&load_bar[w], 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&map_x);
     prefetch_tmap(&map_whi);
     prefetch_tmap(&map_wlo);
     prefetch_tmap(&map_out);
+    if (EPI == EPI_LN) {
+      prefetch_tmap(&map_v);
+      prefetch_tmap(&map_r);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -137,6 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (clustered) cluster_sync();  // the peer's barriers are initialised before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -149,8 +240,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int st = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / args.n_tiles) * BM, n0 = (tile % args.n_tiles) * BN;
+      for (int tile = ts.first; tile < num_tiles && ok; tile += ts.step) {
+        const int m0 = ts.m0(tile), n0 = ts.n0(tile, BN);
         for (int kb = 0; kb < args.k_blocks; ++kb) {
           if (!mbar_wait(&empty[st], phase ^ 1u, abort_flag)) {
             ok = false;
@@ -179,22 +270,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // The whole warp runs the loop with the same values in every lane; one elected lane issues each MMA.
+    {
       constexpr uint32_t idesc = idesc_tf32(BM, BN);
       int st = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
       const uint32_t sb = smem_addr(smem);
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int tile = ts.first; tile < num_tiles && ok; tile += ts.step, ++local) {
         const int as = local % NB;
         const uint32_t acc_phase = (local / NB) & 1u;
-        if (!mbar_wait(&acc_empty[as], acc_phase ^ 1u, abort_flag)) break;
+        if (!mbar_wait_warp(&acc_empty[as], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_main = tmem_base + as * C::kAccCols;
         const uint32_t d_corr = SPLIT ? d_main + BN : d_main;
         for (int kb = 0; kb < args.k_blocks; ++kb) {
-          if (!mbar_wait(&ready[st], phase, abort_flag)) {
+          if (!mbar_wait_warp(&ready[st], phase, abort_flag)) {
             ok = false;
             break;
           }
@@ -207,26 +299,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < C::kBK / 8; ++k) {
             const uint32_t koff = k * 32;  // 8 tf32 = 32 bytes along the swizzled row
             const uint32_t first = (kb == 0 && k == 0) ? 0u : 1u;
-            mma_tf32(d_corr, desc_k<C::kLayout, C::kSbo>(a_lo + koff), desc_k<C::kLayout, C::kSbo>(b_hi + koff),
+            mma_tf32_w(d_corr, desc_k<C::kLayout, C::kSbo>(a_lo + koff), desc_k<C::kLayout, C::kSbo>(b_hi + koff),
                      idesc, first);
-            mma_tf32(d_corr, desc_k<C::kLayout, C::kSbo>(a_hi + koff), desc_k<C::kLayout, C::kSbo>(b_lo + koff),
+            mma_tf32_w(d_corr, desc_k<C::kLayout, C::kSbo>(a_hi + koff), desc_k<C::kLayout, C::kSbo>(b_lo + koff),
                      idesc, 1u);
-            mma_tf32(d_main, desc_k<C::kLayout, C::kSbo>(a_hi + koff), desc_k<C::kLayout, C::kSbo>(b_hi + koff),
+            mma_tf32_w(d_main, desc_k<C::kLayout, C::kSbo>(a_hi + koff), desc_k<C::kLayout, C::kSbo>(b_hi + koff),
                      idesc, SPLIT ? first : 1u);
           }
-          mma_commit(&empty[st]);
+          mma_commit_w(&empty[st]);
           if (++st == S) {
             st = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(&acc_full[as]);
+        mma_commit_w(&acc_full[as]);
       }
-      // Drain: wait for every MMA this thread issued before TMEM is released.
-      mma_commit(mma_done);
+      // Drain: wait for every MMA this warp issued before TMEM is released.
+      mma_commit_w(mma_done);
       volatile int never = 0;
-      if (!mbar_wait(mma_done, 0, &never)) *abort_flag = 1;
+      if (!mbar_wait_warp(mma_done, 0, &never)) *abort_flag = 1;
     }
   } else if (warp < kEpilogueWarp0) {
     // ---------------- x split: hi in place, lo alongside ----------------
@@ -238,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     uint32_t it = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+    for (int tile = ts.first; tile < num_tiles && ok; tile += ts.step) {
       for (int kb = 0; kb < args.k_blocks; ++kb, ++it) {
         if ((it & 1u) == static_cast<uint32_t>(group)) {
           if (!mbar_wait(&full[st], phase, abort_flag)) {
@@ -273,6 +365,219 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  } else if constexpr (EPI == EPI_LN) {
+    // ---------------- epilogue: residual + LayerNorm over whole rows ----------------
+    // Thread (quad, lane) of warp pair `quad` owns row quad*32 + lane of the tile; half h takes the 32-column
+    // chunks c with c % 2 == h, each through the warp's 32x32 staging tile (128-byte swizzle, the layout of the
+    // TMA maps). Pass 1 per chunk: the residual chunk comes in by TMA while the accumulator (+ correction) is
+    // read from TMEM; v = resid + (acc + bias) * scale; running (mean, M2) of the thread's values; v is stored
+    // (if asked) and kept for pass 2 — in TMEM over the accumulator, or, with a single accumulator buffer and v
+    // stored, in the output itself (the accumulator is then released right after pass 1, so the next tile's MMAs
+    // overlap the rest). The two halves combine their statistics in shared memory, the CTAs of a cluster swap
+    // theirs through distributed shared memory (each combines in rank order, so every CTA derives bit-identical
+    // mean and rstd for a row), and pass 2 stores act((v - mean) * rstd * gamma + beta).
+    const int quad = warp & 3;
+    const int half = (warp - kEpilogueWarp0) >> 2;
+    const int ew = warp - kEpilogueWarp0;
+    const int row_t = quad * 32 + lane;
+    uint8_t* stile = store_smem + ew * kStoreTileBytes;
+    uint64_t* lbar = &load_bar[ew];
+    uint32_t lphase = 0;
+    const uint32_t peer = clustered ? (cluster_ctarank() ^ 1u) : 0u;
+    const bool rank0 = !clustered || cluster_ctarank() == 0;
+    const bool v_global = NB == 1 && args.write_v;
+    const float n_half = static_cast<float>(BN / 2);
+    const float inv_n = 1.0f / static_cast<float>(args.N);
+    bool ok = true;
+    // Loads one 32x32 chunk (rows m0 + quad*32.., columns col0..) of `map` into the staging tile, once the
+    // previous bulk operation of this warp on the tile is complete. Returns false if the wait runs out.
+    auto load_chunk = [&](const CUtensorMap* map, int col0, int row0) -> bool {
+      if (lane == 0) bulk_wait<0>();
+      __syncwarp();
+      fence_proxy_async_smem();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(lbar, kStoreTileBytes);
+        tma_load_2d(map, lbar, stile, col0, row0);
+      }
+      const bool done = mbar_wait(lbar, lphase, abort_flag);
+      lphase ^= 1u;
+      return done;
+    };
+    int local = 0;
+    for (int tile = ts.first; tile < num_tiles && ok; tile += ts.step, ++local) {
+      const int as = local % NB;
+      const uint32_t acc_phase = (local / NB) & 1u;
+      if (!mbar_wait(&acc_full[as], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int m0 = ts.m0(tile), n0 = ts.n0(tile, BN);
+      const int row0 = m0 + quad * 32;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + as * C::kAccCols;
+      if (args.resid && tile + ts.step < num_tiles) {  // the residual slices of this thread's next row into L2
+        const int64_t nrow = static_cast<int64_t>(ts.m0(tile + ts.step)) + row_t;
+        if (nrow < args.M)
+          for (int c = half; c < BN / 32; c += 2) {
+            const float* p = args.resid + nrow * args.N + n0 + c * 32;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(p + 31));
+          }
+      }
+      float2 st = make_float2(0.f, 0.f);  // (mean, M2) of the values seen so far
+      float cnt = 0.f;
+#pragma unroll 1
+      for (int c = half; c < BN / 32; c += 2) {
+        const int col0 = n0 + c * 32;
+        if (args.resid) {
+          if (lane == 0) bulk_wait_read<0>();  // the previous store from the staging tile has read it
+          __syncwarp();
+          fence_proxy_async_smem();
+          if (lane == 0) {
+            mbar_arrive_expect_tx(lbar, kStoreTileBytes);
+            tma_load_2d(&map_r, lbar, stile, col0, row0);
+          }
+        } else {
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+        }
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        if constexpr (SPLIT) {
+          uint32_t q[32];
+          tmem_ld_32x32b_x32(taddr + BN + c * 32, q);
+          tmem_ld_wait_regs(r);
+          tmem_ld_wait_regs(q);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
+        } else {
+          tmem_ld_wait_regs(r);
+        }
+        if (args.resid) {
+          ok = mbar_wait(lbar, lphase, abort_flag);
+          lphase ^= 1u;
+          if (!ok) break;
+        }
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int col = col0 + 4 * j;
+          float4* slot = reinterpret_cast<float4*>(stile + lane * 128 + ((j ^ (lane & 7)) << 4));
+          const float4 hv = args.resid ? *slot : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 b = args.bias ? __ldg(reinterpret_cast<const float4*>(args.bias + col))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 sc = args.scale ? __ldg(reinterpret_cast<const float4*>(args.scale + col))
+                                       : make_float4(1.f, 1.f, 1.f, 1.f);
+          float4 v;
+          v.x = hv.x + (__uint_as_float(r[4 * j + 0]) + b.x) * sc.x;
+          v.y = hv.y + (__uint_as_float(r[4 * j + 1]) + b.y) * sc.y;
+          v.z = hv.z + (__uint_as_float(r[4 * j + 2]) + b.z) * sc.z;
+          v.w = hv.w + (__uint_as_float(r[4 * j + 3]) + b.w) * sc.w;
+          r[4 * j + 0] = __float_as_uint(v.x);
+          r[4 * j + 1] = __float_as_uint(v.y);
+          r[4 * j + 2] = __float_as_uint(v.z);
+          r[4 * j + 3] = __float_as_uint(v.w);
+          sum += (v.x + v.y) + (v.z + v.w);
+          if (args.write_v) *slot = v;
+        }
+        const float cm = sum * (1.0f / 32.0f);
+        float m2 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float d = __uint_as_float(r[j]) - cm;
+          m2 += d * d;
+        }
+        if (cnt == 0.f) {
+          st = make_float2(cm, m2);
+        } else {  // Chan: (cnt values) + (32 values)
+          const float tot = cnt + 32.f;
+          const float d = cm - st.x;
+          st.x += d * (32.f / tot);
+          st.y += m2 + d * d * (cnt * 32.f / tot);
+        }
+        cnt += 32.f;
+        if (!v_global) tmem_store_x32(taddr + c * 32, r);
+        if (args.write_v) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_v, stile, col0, row0);
+            bulk_commit();
+          }
+        }
+      }
+      if (!ok) break;
+      if (v_global) {  // v lives in the output now: hand the accumulator back to the MMAs
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[as]);
+      } else {
+        tmem_store_wait();
+      }
+      // Combine the two halves of the row (same order in both warps of the pair).
+      const int par = local & 1;
+      pair_stats[(par * 2 + half) * 128 + row_t] = st;
+      mbar_arrive(&pair_bar[quad]);
+      if (!mbar_wait(&pair_bar[quad], local & 1, abort_flag)) break;
+      st = combine_stats(pair_stats[(par * 2 + 0) * 128 + row_t], pair_stats[(par * 2 + 1) * 128 + row_t], n_half);
+      if (clustered) {
+        if (half == 0) {
+          const uint32_t dst = cluster_map(smem_addr(&peer_stats[par * 128 + row_t]), peer);
+          cluster_store_f2(dst, st.x, st.y);
+          mbar_arrive_cluster(cluster_map(smem_addr(&peer_bar[par]), peer));
+        }
+        if (!mbar_wait_cluster(&peer_bar[par], (local >> 1) & 1, abort_flag)) break;
+        const float2 other = peer_stats[par * 128 + row_t];
+        st = rank0 ? combine_stats(st, other, static_cast<float>(BN)) : combine_stats(other, st, static_cast<float>(BN));
+      }
+      const float mean = st.x;
+      const float rstd = 1.0f / sqrtf(st.y * inv_n + args.eps);
+#pragma unroll 1
+      for (int c = half; c < BN / 32; c += 2) {
+        const int col0 = n0 + c * 32;
+        uint32_t r[32];
+        if (v_global) {
+          // v of this chunk was stored by this warp in pass 1; bulk_wait<0> inside load_chunk makes that store
+          // complete before the load is issued
+          if (!(ok = load_chunk(&map_v, col0, row0))) break;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 v = *reinterpret_cast<const float4*>(stile + lane * 128 + ((j ^ (lane & 7)) << 4));
+            r[4 * j + 0] = __float_as_uint(v.x);
+            r[4 * j + 1] = __float_as_uint(v.y);
+            r[4 * j + 2] = __float_as_uint(v.z);
+            r[4 * j + 3] = __float_as_uint(v.w);
+          }
+        } else {
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          tmem_ld_wait_regs(r);
+          if (c + 2 >= BN / 32) {  // this warp's last read of the tile: release the accumulator
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[as]);
+          }
+          if (lane == 0) bulk_wait_read<0>();
+        }
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int col = col0 + 4 * j;
+          const float4 g = __ldg(reinterpret_cast<const float4*>(args.gamma + col));
+          const float4 bt = __ldg(reinterpret_cast<const float4*>(args.beta + col));
+          float4 o;
+          o.x = ln_act((__uint_as_float(r[4 * j + 0]) - mean) * rstd * g.x + bt.x, args.act);
+          o.y = ln_act((__uint_as_float(r[4 * j + 1]) - mean) * rstd * g.y + bt.y, args.act);
+          o.z = ln_act((__uint_as_float(r[4 * j + 2]) - mean) * rstd * g.z + bt.z, args.act);
+          o.w = ln_act((__uint_as_float(r[4 * j + 3]) - mean) * rstd * g.w + bt.w, args.act);
+          *reinterpret_cast<float4*>(stile + lane * 128 + ((j ^ (lane & 7)) << 4)) = o;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_out, stile, col0, row0);
+          bulk_commit();
+        }
+      }
+    }
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
   } else {
     // ---------------- epilogue ----------------
     // Warp pair per TMEM lane quadrant; half h of the pair takes the 32-column chunks c with c % 2 == h. Each
@@ -282,12 +587,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - kEpilogueWarp0) >> 2;
     uint8_t* stile = store_smem + (warp - kEpilogueWarp0) * kStoreTileBytes;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int tile = ts.first; tile < num_tiles; tile += ts.step, ++local) {
       const int as = local % NB;
       const uint32_t acc_phase = (local / NB) & 1u;
       if (!mbar_wait(&acc_full[as], acc_phase, abort_flag)) break;
       tc_fence_after();
-      const int m0 = (tile / args.n_tiles) * BM, n0 = (tile % args.n_tiles) * BN;
+      const int m0 = ts.m0(tile), n0 = ts.n0(tile, BN);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + as * C::kAccCols;
 #pragma unroll 1
       for (int c = half; c < BN / 32; c += 2) {
@@ -337,6 +642,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   }
 
+  __syncwarp();
+  if (clustered) cluster_sync();  // no CTA leaves while its peer may still write into its shared memory
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -377,7 +684,7 @@ namespace {
 template <int BN, int BKB, bool SPLIT>
 int launch_gemm(const float* x, const float* w_packed, const float* bias, int64_t M, int64_t K, int64_t N,
                 int act, float* out, int* dev_status, cudaStream_t stream) {
-  using C = Cfg<BN, BKB, SPLIT>;
+  using C = Cfg<BN, BKB, SPLIT, EPI_ACT>;
   const CUtensorMapSwizzle sw = BKB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   CUtensorMap mx, mhi, mlo;
   int st = ko::make_tmap_2d_f32(&mx, x, M, K, K, BM, C::kBK, sw, "ko_linear x");
@@ -392,10 +699,10 @@ int launch_gemm(const float* x, const float* w_packed, const float* bias, int64_
   const ko::DeviceInfo& info = ko::device_info();
   if (static_cast<int64_t>(C::kSmemBytes) > info.max_smem_optin)
     return ko::fail(KO_ERR_UNSUPPORTED, "ko_linear: not enough shared memory on this device");
-  cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BKB, SPLIT>,
+  cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BKB, SPLIT, EPI_ACT>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmemBytes));
   if (e != cudaSuccess) return ko::fail(static_cast<int>(e), "ko_linear: cudaFuncSetAttribute failed");
-  GemmArgs a;
+  GemmArgs a = {};
   a.bias = bias;
   a.out = out;
   a.dev_status = dev_status;
@@ -408,8 +715,95 @@ int launch_gemm(const float* x, const float* w_packed, const float* bias, int64_
   a.k_blocks = static_cast<int>((K + C::kBK - 1) / C::kBK);
   const int tiles = a.m_tiles * a.n_tiles;
   const int grid = std::min(tiles, info.sm_count);
-  gemm_tf32x3_kernel<BN, BKB, SPLIT><<<grid, kThreads, C::kSmemBytes, stream>>>(mx, mhi, mlo, mout, a);
+  a.cs = 1;
+  gemm_tf32x3_kernel<BN, BKB, SPLIT, EPI_ACT><<<grid, kThreads, C::kSmemBytes, stream>>>(mx, mhi, mlo, mout, mout, mout, a);
   return ko::check_launch("ko_linear_f32_packed");
+}
+
+// GEMM + residual + LayerNorm: clusters of cs = N / BN CTAs, one row block per cluster at a time.
+template <int BN, bool SPLIT>
+int launch_gemm_ln(const float* x, const float* w_packed, const float* bias, const float* scale, const float* resid,
+                   const float* gamma, const float* beta, float eps, int64_t M, int64_t K, int64_t N, int act,
+                   float* v_out, float* y, int* dev_status, cudaStream_t stream) {
+  constexpr int BKB = 64;
+  using C = Cfg<BN, BKB, SPLIT, EPI_LN>;
+  const int cs = static_cast<int>(N / BN);
+  const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_64B;
+  CUtensorMap mx, mhi, mlo, my, mv;
+  int st = ko::make_tmap_2d_f32(&mx, x, M, K, K, BM, C::kBK, sw, "ko_linear_residual_ln x");
+  if (st) return st;
+  st = ko::make_tmap_2d_f32(&mhi, w_packed, N, K, K, BN, C::kBK, sw, "ko_linear_residual_ln w_hi");
+  if (st) return st;
+  st = ko::make_tmap_2d_f32(&mlo, w_packed + N * K, N, K, K, BN, C::kBK, sw, "ko_linear_residual_ln w_lo");
+  if (st) return st;
+  st = ko::make_tmap_2d_f32(&my, y, M, N, N, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, "ko_linear_residual_ln y");
+  if (st) return st;
+  st = ko::make_tmap_2d_f32(&mv, v_out ? v_out : y, M, N, N, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+                            "ko_linear_residual_ln h_out");
+  if (st) return st;
+  CUtensorMap mr;
+  st = ko::make_tmap_2d_f32(&mr, resid ? resid : y, M, N, N, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+                            "ko_linear_residual_ln resid");
+  if (st) return st;
+  const ko::DeviceInfo& info = ko::device_info();
+  if (static_cast<int64_t>(C::kSmemBytes) > info.max_smem_optin)
+    return ko::fail(KO_ERR_UNSUPPORTED, "ko_linear_residual_ln: not enough shared memory on this device");
+  auto kernel = gemm_tf32x3_kernel<BN, BKB, SPLIT, EPI_LN>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmemBytes));
+  if (e != cudaSuccess) return ko::fail(static_cast<int>(e), "ko_linear_residual_ln: cudaFuncSetAttribute failed");
+  GemmArgs a = {};
+  a.bias = bias;
+  a.out = y;
+  a.dev_status = dev_status;
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.act = act;
+  a.m_tiles = static_cast<int>((M + BM - 1) / BM);
+  a.n_tiles = cs;
+  a.k_blocks = static_cast<int>((K + C::kBK - 1) / C::kBK);
+  a.scale = scale;
+  a.resid = resid;
+  a.gamma = gamma;
+  a.beta = beta;
+  a.eps = eps;
+  a.write_v = v_out != nullptr;
+  a.cs = cs;
+
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cs);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // As many clusters as fit at once (one CTA per SM; SMs a GPC cannot pair up stay idle), at most one per row
+  // block; each cluster then strides over the row blocks.
+  static std::atomic<int> max_clusters[2][64];  // per cluster size and device, looked up once
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::atomic<int>& slot = max_clusters[cs - 1][dev & 63];
+  int mc = slot.load();
+  if (mc == 0) {
+    cfg.gridDim = dim3(static_cast<unsigned>(info.sm_count / cs * cs));
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+    if (e != cudaSuccess || n < 1)
+      return ko::fail(e != cudaSuccess ? static_cast<int>(e) : KO_ERR_UNSUPPORTED,
+                      "ko_linear_residual_ln: no cluster of this size fits on the device");
+    mc = n;
+    slot.store(n);
+  }
+  const int clusters = std::min(a.m_tiles, mc);
+  cfg.gridDim = dim3(static_cast<unsigned>(clusters * cs));
+  e = cudaLaunchKernelEx(&cfg, kernel, mx, mhi, mlo, my, mv, mr, a);
+  if (e != cudaSuccess) return ko::fail(static_cast<int>(e), "ko_linear_residual_ln: launch failed");
+  return ko::check_launch("ko_linear_residual_ln_f32_packed");
 }
 
 using LaunchFn = int (*)(const float*, const float*, const float*, int64_t, int64_t, int64_t, int, float*, int*,
@@ -507,6 +901,42 @@ extern "C" int ko_linear_f32_packed(const float* x, const float* w_packed, const
     return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_linear_f32_packed: unknown activation");
   const Variant* v = choose_variant(M, N, K);
   return v->fn(x, w_packed, bias, M, K, N, act, out, dev_status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ko_linear_residual_ln_f32_packed(const float* x, const float* w_packed, const float* bias,
+                                                const float* scale, const float* resid, const float* gamma,
+                                                const float* beta, float eps, int64_t M, int64_t K, int64_t N,
+                                                int act, float* h_out, float* y, int* dev_status,
+                                                ko_stream_t stream) {
+  const char* who = "ko_linear_residual_ln_f32_packed";
+  int st = validate_linear(x, w_packed, bias, M, K, N, y, who);
+  if (st || M == 0) return st;
+  if (N != 128 && N != 192 && N != 256 && N != 384 && N != 512)
+    return ko::fail(KO_ERR_UNSUPPORTED, std::string(who) + ": N must be 128, 192, 256, 384 or 512 (whole rows in "
+                                                           "one CTA or a pair of CTAs)");
+  if (act != KO_ACT_NONE && act != KO_ACT_SILU)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": act must be KO_ACT_NONE or KO_ACT_SILU");
+  if (!gamma || !beta || !(eps >= 0.0f))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": gamma and beta are required, eps >= 0");
+  if (!ko::aligned16(gamma) || !ko::aligned16(beta) || (scale && !ko::aligned16(scale)) ||
+      (resid && !ko::aligned16(resid)) || (h_out && !ko::aligned16(h_out)))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": pointers must be 16-byte aligned");
+  if (y == resid || y == h_out || y == x)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": y must not alias x, resid or h_out");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool split = K > 512;
+  const int bn = N == 384 ? 192 : N == 512 ? 256 : static_cast<int>(N);
+#define KO_LN_CASE(BNV)                                                                                         \
+  if (bn == BNV)                                                                                               \
+    return split ? launch_gemm_ln<BNV, true>(x, w_packed, bias, scale, resid, gamma, beta, eps, M, K, N, act,   \
+                                             h_out, y, dev_status, s)                                          \
+                 : launch_gemm_ln<BNV, false>(x, w_packed, bias, scale, resid, gamma, beta, eps, M, K, N, act,  \
+                                              h_out, y, dev_status, s);
+  KO_LN_CASE(128)
+  KO_LN_CASE(192)
+  KO_LN_CASE(256)
+#undef KO_LN_CASE
+  return ko::fail(KO_ERR_UNSUPPORTED, std::string(who) + ": no tile for this N");
 }
 
 extern "C" int ko_linear_gelu_f32(const float* x, const float* w, const float* bias, int64_t M, int64_t K,

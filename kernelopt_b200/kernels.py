@@ -257,6 +257,43 @@ def linear(x, pw: PackedWeight, act=None, out=None):
     return out
 
 
+LN_WIDTHS = (128, 192, 256, 384, 512)
+
+
+def linear_residual_layernorm(x, pw: PackedWeight, gamma, beta, eps, resid=None, scale=None, act=None,
+                              h_out=None, y=None, write_h=True):
+    """One GEMM with the residual add and LayerNorm in its epilogue:
+        h_out = resid + (x @ W + bias) * scale;   y = act(LayerNorm(h_out) * gamma + beta)
+    bias is the PackedWeight's (None = 0), scale None = 1, resid None = no residual, act None or 'silu'.
+    Returns (h_out, y); h_out is None when write_h is False. h_out may be resid (in place). W's width must be
+    one of LN_WIDTHS. Fuses the reference's out-projection / fc2 GEMM + residual_layernorm pairs
+    (model.py:121-123, 129-132) and the projector's conv GEMM + LayerNorm + SiLU (model.py:148-158)."""
+    _need(x, "x")
+    if x.shape[-1] != pw.k:
+        raise ValueError(f"x has {x.shape[-1]} features, the weight expects {pw.k}")
+    n = pw.n
+    if n not in LN_WIDTHS:
+        raise ValueError(f"output width {n} is not one of {LN_WIDTHS}")
+    for name, t in (("gamma", gamma), ("beta", beta), ("scale", scale)):
+        if t is not None and _need(t, name).numel() != n:
+            raise ValueError(f"{name} must have {n} elements")
+    if act not in (None, "none", "silu"):
+        raise ValueError("act must be None or 'silu'")
+    shape = (*x.shape[:-1], n)
+    if resid is not None and tuple(_need(resid, "resid").shape) != shape:
+        raise ValueError(f"resid must have shape {shape}")
+    m = x.numel() // pw.k
+    if y is None:
+        y = torch.empty(shape, dtype=torch.float32, device=x.device)
+    if write_h and h_out is None:
+        h_out = torch.empty(shape, dtype=torch.float32, device=x.device)
+    call("ko_linear_residual_ln_f32_packed", x.data_ptr(), pw.packed.data_ptr(), _ptr(pw.bias), _ptr(scale),
+         _ptr(resid), gamma.data_ptr(), beta.data_ptr(), float(eps), m, pw.k, n,
+         _lib.KO_ACT_SILU if act == "silu" else _lib.KO_ACT_NONE, _ptr(h_out if write_h else None), y.data_ptr(),
+         status_word(x.device).data_ptr(), _stream())
+    return (h_out if write_h else None), y
+
+
 _pack_cache: "weakref.WeakKeyDictionary[torch.Tensor, tuple[int, PackedWeight]]" = weakref.WeakKeyDictionary()
 _pack_lock = threading.Lock()
 

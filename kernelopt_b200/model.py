@@ -2,8 +2,10 @@
 the hot path on libkernelopt's sm_100a kernels.
 
 Call sites of the reference's kernels (model.py:122, 125, 131, 226) use the same kernels here:
-  residual_layernorm   after the attention out-projection and after fc2 (24 calls per frame); the decoder's
-                       post-norms LN(tgt + x) use it too (12 calls per frame, no bias/scale)
+  residual_layernorm   after the attention out-projection and after fc2 (24 calls per frame) — here inside the
+                       epilogue of those two GEMMs (ko_linear_residual_ln: the reference's listed next step); the
+                       decoder's post-norms LN(tgt + linear(x)), the projector's conv GEMM -> LN -> SiLU and the
+                       encoder-output linear + LN run through the same fused kernel
   linear_gelu_f32      backbone fc1 (the 3xTF32 tcgen05 GEMM with the GELU epilogue)
   deform_attn          decoder cross-attention sampling, on the one fused [B,1600,1024] value projection
 Every other dense layer (QKV, out-proj, fc2, the patch embedding, the projector's 1x1 and im2col'd 3x3 convs,
@@ -11,7 +13,8 @@ the decoder linears) runs on the same fp32-grade tcgen05 GEMM; only the layers w
 multiple of 4 (11 classes, 4 box coordinates) use torch's fp32 matmul. Attention — the backbone's windowed and
 global self-attention and the decoder's self-attention (the reference's mx.fast.scaled_dot_product_attention) — runs
 on the fp32-grade 3xTF32 tcgen05 flash-attention kernel, straight on column slices of the fused QKV projection.
-LayerNorms outside the fused sites, SiLU, softmax and top-300 are torch ops in fp32 with TF32 disabled.
+The remaining LayerNorms run on the LayerNorm kernel; softmax and top-300 are torch ops in fp32 with TF32
+disabled.
 
 The input is the patch layout the preprocessing kernel writes (PATCH16: [B, 1600, 768]), which makes the
 16x16/16 patch-embedding convolution one GEMM; NHWC [B, 640, 640, 3] (the reference's input) is accepted too.
@@ -32,6 +35,7 @@ FULL_ATTN = (3, 6, 9)
 TAPS = (2, 5, 8, 11)
 GRID, WIN, C, HEADS = 40, 20, 384, 6
 D_MODEL, SA_HEADS, N_QUERIES = 256, 8, 300
+FUSED_LN_MAX_ROWS_WIDE_K = 148 * 128 * 2  # up to two waves of row blocks the serialised epilogue is cheaper
 
 
 def configure_numerics() -> None:
@@ -51,6 +55,28 @@ class Dense:
             self.pw = K.pack_weight(w.contiguous(), None if b is None else b.contiguous())
         else:
             self.w, self.b = w.contiguous(), b
+
+    def ln(self, x: torch.Tensor, ln, resid=None, scale=None, act=None, write_h=None):
+        """(h_out, y) with h_out = resid + (x @ W + b) * scale and y = act(LayerNorm(h_out)): one GEMM whose
+        epilogue does the residual add and the LayerNorm when the output width allows it (ko_linear_residual_ln),
+        else the GEMM and then the LayerNorm kernel. h_out is returned only when there is a residual."""
+        w, b, eps = ln
+        if write_h is None:
+            write_h = resid is not None
+        # K > 512 needs the correction accumulator, which leaves TMEM for one accumulator buffer: the fused
+        # epilogue then cannot overlap the next tile's MMAs and, over many row blocks, the separate LayerNorm
+        # kernel is faster (fc2 at 102 656 rows: 709 us fused against 685 us for the pair on B200).
+        rows = x.numel() // self.k
+        fuse = self.k <= 512 or rows <= FUSED_LN_MAX_ROWS_WIDE_K
+        if self.native and self.n in K.LN_WIDTHS and fuse:
+            return K.linear_residual_layernorm(x.contiguous(), self.pw, w, b, eps, resid=resid, scale=scale,
+                                               act=act, write_h=write_h)
+        o = self(x)
+        if resid is None and scale is None:
+            return None, K.layernorm(o.contiguous(), w, b, eps, act)
+        h = torch.zeros_like(o) if resid is None else resid
+        h_out, y = K.residual_layernorm(h.contiguous(), o.contiguous(), None, scale, w, b, eps)
+        return h_out, (K.layernorm(h_out, w, b, eps, act) if act else y)
 
     def __call__(self, x: torch.Tensor, act=None) -> torch.Tensor:
         if self.native:
@@ -102,12 +128,12 @@ class RFDETR:
             nxt = LAYER.format(i + 1) + "norm1" if i < 11 else BB + "layernorm"
             self.layers.append(dict(
                 qkv=Dense(wqkv, bqkv),
-                out=Dense(p[pre + "attention.output.dense.weight"], None),
-                out_b=p[pre + "attention.output.dense.bias"], ls1=p[pre + "layer_scale1.lambda1"],
+                out=Dense(p[pre + "attention.output.dense.weight"], p[pre + "attention.output.dense.bias"]),
+                ls1=p[pre + "layer_scale1.lambda1"],
                 norm2=self._ln(pre + "norm2"),
                 fc1=K.pack_weight(p[pre + "mlp.fc1.weight"], p[pre + "mlp.fc1.bias"]),
-                fc2=Dense(p[pre + "mlp.fc2.weight"], None),
-                fc2_b=p[pre + "mlp.fc2.bias"], ls2=p[pre + "layer_scale2.lambda1"],
+                fc2=Dense(p[pre + "mlp.fc2.weight"], p[pre + "mlp.fc2.bias"]),
+                ls2=p[pre + "layer_scale2.lambda1"],
                 next_norm=self._ln(nxt)))
         self.norm1_0 = self._ln(LAYER.format(0) + "norm1")
         self.final_ln = self._ln(BB + "layernorm")
@@ -180,13 +206,10 @@ class RFDETR:
         nb, Lb = (b, 4 * L) if i in FULL_ATTN else (n, L)                                      # global: merge windows
         qkv = lyr["qkv"](y.reshape(nb * Lb, C)).reshape(nb, Lb, 3 * C)                         # q | k | v columns
         o = K.attention(qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:], HEADS, 1 / math.sqrt(C // HEADS))
-        o = lyr["out"](o.reshape(n * L, C)).reshape(n, L, C)
-        w2, b2, e2 = lyr["norm2"]
-        h, y = K.residual_layernorm(h, o, lyr["out_b"], lyr["ls1"], w2, b2, e2)
+        # out-projection + bias, * layer scale, + residual, norm2: one kernel (and fc2 + next norm1 likewise)
+        h, y = lyr["out"].ln(o.reshape(n, L, C), lyr["norm2"], resid=h, scale=lyr["ls1"])
         m = K.linear(y, lyr["fc1"], "gelu")
-        o = lyr["fc2"](m)
-        wn, bn, en = lyr["next_norm"]
-        return K.residual_layernorm(h, o, lyr["fc2_b"], lyr["ls2"], wn, bn, en)
+        return lyr["fc2"].ln(m, lyr["next_norm"], resid=h, scale=lyr["ls2"])
 
     # ---- projector ----------------------------------------------------------------------------------------
     def _convx(self, x, cv):
@@ -196,8 +219,8 @@ class RFDETR:
             cols = x.reshape(b * hh * ww, cin)
         else:
             cols = K.im2col3x3(x.contiguous())                                                   # [B*H*W, 9*cin]
-        y = cv["dense"](cols)
-        return self._ln_op(y, cv["ln"], "silu").reshape(b, hh, ww, -1)
+        _, y = cv["dense"].ln(cols, cv["ln"], act="silu")                                     # GEMM + LN + SiLU
+        return y.reshape(b, hh, ww, -1)
 
     def projector(self, feats):
         y = self._convx(torch.cat(feats, -1), self.cv1)
@@ -216,7 +239,7 @@ class RFDETR:
     def select_queries(self, memory):
         """model.py:175-185: class score per proposal, box refinement, top-300 by score."""
         om = memory * self.valid
-        om = self._ln_op(self.enc_output(om), self.enc_norm)
+        _, om = self.enc_output.ln(om, self.enc_norm)
         scores = self.enc_class(om).amax(-1)                                                    # [B, 1600]
         delta = self._mlp3(om, self.enc_bbox)
         prop = self.props
@@ -234,10 +257,6 @@ class RFDETR:
             outs.append(torch.stack([torch.sin(v[..., 0::2]), torch.cos(v[..., 1::2])], -1).reshape(*v.shape[:2], 128))
         return torch.cat(outs, -1)
 
-    def _add_ln(self, x, r, ln):
-        w, b, eps = ln
-        return K.residual_layernorm(x.contiguous(), r.contiguous(), None, None, w, b, eps)[1]
-
     def decoder(self, memory, ref):
         b = memory.shape[0]
         qpos = self.rph[1](self.rph[0](self.sine_embed(ref), "relu"))
@@ -248,17 +267,15 @@ class RFDETR:
             qk = lyr["qk"](tgt + qpos).reshape(b, N_QUERIES, 2 * D_MODEL)                      # q | k columns
             v = lyr["v"](tgt).reshape(b, N_QUERIES, D_MODEL)
             o = K.attention(qk[..., :D_MODEL], qk[..., D_MODEL:], v, SA_HEADS, 1 / math.sqrt(hd))
-            sa = lyr["out"](o)
-            tgt = self._add_ln(tgt, sa, lyr["norm1"])
+            _, tgt = lyr["out"].ln(o, lyr["norm1"], resid=tgt, write_h=False)                  # LN(tgt + out(o))
             oa = lyr["offaw"](tgt + qpos)                                                         # [B, 300, 96]
             off = oa[..., :CA_HEADS * CA_POINTS * 2].reshape(b, N_QUERIES, CA_HEADS, CA_POINTS, 2)
             aw = torch.softmax(oa[..., CA_HEADS * CA_POINTS * 2:].reshape(b, N_QUERIES, CA_HEADS, CA_POINTS), -1)
             r = ref[:, :, None, None, :]
             loc = r[..., :2] + off / CA_POINTS * r[..., 2:] * 0.5
             s = K.deform_attn(values, loc, aw, (GRID, GRID), CA_HEADS, D_MODEL // CA_HEADS, offset=i * D_MODEL)
-            tgt = self._add_ln(tgt, lyr["oproj"](s), lyr["norm2"])
-            ffn = lyr["l2"](lyr["l1"](tgt, "relu"))
-            tgt = self._add_ln(tgt, ffn, lyr["norm3"])
+            _, tgt = lyr["oproj"].ln(s, lyr["norm2"], resid=tgt, write_h=False)
+            _, tgt = lyr["l2"].ln(lyr["l1"](tgt, "relu"), lyr["norm3"], resid=tgt, write_h=False)
         return self._ln_op(tgt, self.dec_norm)
 
     # ---- full forward -------------------------------------------------------------------------------------------

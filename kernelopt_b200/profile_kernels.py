@@ -11,6 +11,9 @@ Kernels and workloads (per frame of batch B; the algorithmic traffic or flops co
   attn        the backbone's global attention: B frames x 1604 tokens x 6 heads x 64, q/k/v column slices of
               one [B, 1604, 1152] projection ~ N(0,1); flops = 4 * B * 6 * 1604^2 * 64
   attn_win    the windowed attention: 4B windows x 401 tokens x 6 heads x 64; flops = 4 * 4B * 6 * 401^2 * 64
+  outproj_ln  the out-projection + bias, * layer scale, + residual, LayerNorm in one kernel: x [B*1604, 384],
+              W [384, 384]; flops = 2*M*384*384 (outproj_unfused: the GEMM, then the residual + LN kernel)
+  fc2_ln      the same for fc2: x [B*1604, 1536], W [1536, 384] (fc2_unfused likewise)
 Each timed iteration is preceded, outside the events, by a write and a read-back of a 256 MB buffer (larger
 than the 126 MB L2): every launch starts with a cold L2 that holds no dirty lines of the flush (their write-back
 would otherwise be charged to the timed kernel), and a short spin kernel holds the stream while the host enqueues the
@@ -61,6 +64,22 @@ def setup(kernel: str, b: int, dev):
         bias = (0.01 * torch.randn(1536, generator=g)).to(dev)
         pw = K.pack_weight(w, bias)
         return (lambda: K.linear(a, pw, "gelu")), 2.0 * m * 384 * 1536, "flop"
+    if kernel in ("outproj_ln", "outproj_unfused", "fc2_ln", "fc2_unfused"):
+        m, k = b * 1604, (384 if kernel.startswith("outproj") else 1536)
+        x = torch.randn(m, k, generator=g).to(dev)
+        w = (torch.randn(k, 384, generator=g) / k ** 0.5).to(dev)
+        bias = (0.1 * torch.randn(384, generator=g)).to(dev)
+        scale = (1 + 0.1 * torch.randn(384, generator=g)).to(dev)
+        h = torch.randn(m, 384, generator=g).to(dev)
+        gamma = (1 + 0.1 * torch.randn(384, generator=g)).to(dev)
+        beta = (0.1 * torch.randn(384, generator=g)).to(dev)
+        if kernel.endswith("_ln"):
+            pw = K.pack_weight(w, bias)
+            fn = lambda: K.linear_residual_layernorm(x, pw, gamma, beta, 1e-6, resid=h, scale=scale)  # noqa: E731
+        else:
+            pw = K.pack_weight(w)
+            fn = lambda: K.residual_layernorm(h, K.linear(x, pw), bias, scale, gamma, beta, 1e-6)  # noqa: E731
+        return fn, 2.0 * m * k * 384, "flop"
     if kernel == "deform":
         value = torch.randn(b, 1600, 256, generator=g).to(dev)
         loc = (torch.rand(b, 300, 16, 2, 2, generator=g) * 1.1 - 0.05).to(dev)
@@ -76,7 +95,8 @@ def setup(kernel: str, b: int, dev):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", required=True, choices=["preprocess", "resln", "gemm", "deform", "attn", "attn_win"])
+    ap.add_argument("--kernel", required=True, choices=["preprocess", "resln", "gemm", "deform", "attn", "attn_win",
+                                                             "outproj_ln", "outproj_unfused", "fc2_ln", "fc2_unfused"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)

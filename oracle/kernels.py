@@ -48,6 +48,19 @@ def linear_gelu_f32(x, w, bias):
     return linear(x, w, bias, "gelu")
 
 
+def linear_residual_layernorm(x, w, bias, scale, resid, gamma, beta, eps, act=None):
+    """The GEMM followed by residual_layernorm, as the reference runs them one after the other: the attention
+    out-projection / fc2 GEMM, then h + (o + bias) * scale and its LayerNorm (model.py:121-123, 129-132,
+    kernels.py:53-67); without a residual and with act='silu', the projector's conv GEMM -> channel LayerNorm ->
+    SiLU (model.py:148-158). Returns (h_out, y)."""
+    o = linear(x, w)
+    h = np.zeros_like(o) if resid is None else np.asarray(resid, np.float64)
+    h_out, y = residual_layernorm(h, o, bias, scale, gamma, beta, eps)
+    if act == "silu":
+        y = y / (1.0 + np.exp(-y))
+    return h_out, y
+
+
 def deform_attn(value, loc, aw, grid_hw, nh, hd, offset=0):
     """out[b,q,h*hd+d] = sum_p aw * bilinear(value[b, :, offset + h*hd + d] as GH x GW, loc) — kernels.py:165-181
     and model.py:196-216 + 228-229 (GridSample, zero padding, align_corners=False).

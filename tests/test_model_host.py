@@ -55,6 +55,13 @@ def _layernorm(x, g, b, eps, act=None, out=None):
     return F.silu(y) if act == "silu" else y
 
 
+def _lrln(x, pw, gamma, beta, eps, resid=None, scale=None, act=None, h_out=None, y=None, write_h=True):
+    o = _linear(x, pw)
+    ho = (0 if resid is None else resid) + o * (1 if scale is None else scale)
+    yy = F.layer_norm(ho, (ho.shape[-1],), gamma, beta, eps)
+    return (ho if write_h else None), (F.silu(yy) if act == "silu" else yy)
+
+
 def _im2col3x3(x, out=None):
     b, h, w, c = x.shape
     xp = F.pad(x, (0, 0, 1, 1, 1, 1))
@@ -72,6 +79,7 @@ def cpu_model(monkeypatch):
     monkeypatch.setattr(K, "attention", _attention)
     monkeypatch.setattr(K, "layernorm", _layernorm)
     monkeypatch.setattr(K, "im2col3x3", _im2col3x3)
+    monkeypatch.setattr(K, "linear_residual_layernorm", _lrln)
     monkeypatch.setattr(K, "status_word", lambda *a: None)
     w = random_weights(0)
 

@@ -270,9 +270,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
     }
   } else if (warp < kLoadWarp0) {
     // ---------------- softmax + output, one thread per query row ----------------
-    // Block j: max of S_j (pass 1); then, once P_{j-1}.V_{j-1}'s P_lo products are done (the P_lo columns are
-    // free), P_j = exp2(S_j * c - m) as hi / lo into tensor memory (pass 2); then, once all of P_{j-1}.V_{j-1} is
-    // complete, o = o * alpha + that block's product.
+    // Block j, one pass over S_j: once P_{j-1}.V_{j-1}'s P_lo products are done (the P_lo columns are free), each
+    // 16-key chunk becomes P = exp2(S * c - m) as tf32 hi / lo in tensor memory. The exponent offset m is raised
+    // lazily: only when a chunk's maximum exceeds it by more than kRaise (so P <= 2^kRaise), and then the chunks
+    // of this block already written are rescaled in place. The final o / l is the same for any offset, since
+    // numerator and denominator share it. Then, once all of P_{j-1}.V_{j-1} is complete, o = o * alpha + that
+    // block's product.
+    constexpr float kRaise = 8.0f;
     const int quad = warp & 3;  // tensor-memory lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
@@ -303,38 +307,64 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
         ok = false;
         break;
       }
+      if (j >= 1 && !warp_wait(plo_free, static_cast<uint32_t>(j - 1) & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const uint32_t srow = trow + kColS + static_cast<uint32_t>(j & 1) * BKEY;
+      const uint32_t plrow = trow + kColPlo;
       const int valid = min(BKEY, a.L - j * BKEY);
       const int chunks = (valid + 15) >> 4;  // 16-column chunks that hold keys of this block
-      float mb = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < chunks; ++c) {
-        uint32_t r[16];
-        tmem_ld_32x32b_x16(srow + 16 * c, r);
-        tmem_ld_wait_regs16(r);
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          if (16 * c + e < valid) mb = fmaxf(mb, __uint_as_float(r[e]));
-      }
-      const float m_new = fmaxf(m, mb * a.scale_log2);
-      const float alpha = fast_exp2(m - m_new);
-      if (j >= 1) {
-        if (!warp_wait(plo_free, static_cast<uint32_t>(j - 1) & 1u, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-      }
+      float mb = m;                          // offset of this block's P
       float ls = 0.f;
 #pragma unroll 1
       for (int c = 0; c < chunks; ++c) {
         uint32_t r[16], lo[16];
         tmem_ld_32x32b_x16(srow + 16 * c, r);
         tmem_ld_wait_regs16(r);
+        const int nv = valid - 16 * c;  // keys of this chunk (>= 16 except in a short last block)
+        if (nv < 16) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (e >= nv) r[e] = __float_as_uint(-INFINITY);
+        }
+        float c0 = fmaxf(__uint_as_float(r[0]), __uint_as_float(r[1]));
+        float c1 = fmaxf(__uint_as_float(r[2]), __uint_as_float(r[3]));
+#pragma unroll
+        for (int e = 4; e < 16; e += 4) {
+          c0 = fmaxf(c0, fmaxf(__uint_as_float(r[e]), __uint_as_float(r[e + 1])));
+          c1 = fmaxf(c1, fmaxf(__uint_as_float(r[e + 2]), __uint_as_float(r[e + 3])));
+        }
+        const float cmax = fmaxf(c0, c1) * a.scale_log2;
+        const bool raise = cmax > mb + kRaise;
+        if (__any_sync(0xffffffffu, raise)) {  // rare after the first chunk: raise the offset, rescale chunks < c
+          const float m_new = raise ? cmax : mb;
+          const float beta = fast_exp2(mb - m_new);  // 0 when mb was -inf (nothing written yet)
+          tmem_st_wait();
+#pragma unroll 1
+          for (int cc = 0; cc < c; ++cc) {
+            uint32_t h2[16], l2[16];
+            tmem_ld_32x32b_x16(srow + 16 * cc, h2);
+            tmem_ld_32x32b_x16(plrow + 16 * cc, l2);
+            tmem_ld_wait_regs16(h2);
+            tmem_ld_wait_regs16(l2);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              float phi, plo;
+              split_tf32((__uint_as_float(h2[e]) + __uint_as_float(l2[e])) * beta, phi, plo);
+              h2[e] = __float_as_uint(phi);
+              l2[e] = __float_as_uint(plo);
+            }
+            tmem_st_32x32b_x16(srow + 16 * cc, h2);
+            tmem_st_32x32b_x16(plrow + 16 * cc, l2);
+          }
+          ls *= beta;
+          mb = m_new;
+        }
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p = (16 * c + e < valid) ? fast_exp2(fmaf(__uint_as_float(r[e]), a.scale_log2, -m_new)) : 0.f;
+          const float p = fast_exp2(fmaf(__uint_as_float(r[e]), a.scale_log2, -mb));  // 0 for masked keys
           ls += p;
           float phi, plo;
           split_tf32(p, phi, plo);
@@ -342,11 +372,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
           lo[e] = __float_as_uint(plo);
         }
         tmem_st_32x32b_x16(srow + 16 * c, r);
-        tmem_st_32x32b_x16(trow + kColPlo + 16 * c, lo);
+        tmem_st_32x32b_x16(plrow + 16 * c, lo);
       }
       tmem_st_wait();
+      const float alpha = fast_exp2(m - mb);  // 0 for the first block (m = -inf)
       l = l * alpha + ls;
-      m = m_new;
+      m = mb;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);

@@ -100,9 +100,12 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// v = hi + lo with hi = tf32_rn(v). lo = v - hi is exact in fp32 and is left unrounded: the tensor core reads a
+// tf32 operand from its top 19 bits, so lo enters the product truncated to tf32, an error below 2^-21 |v|
+// (2^-22 with lo rounded first), which saves the second rounding's two integer operations.
 __device__ __forceinline__ void split_tf32(float v, float& hi, float& lo) {
   hi = __uint_as_float(f32_to_tf32_rna_int(v));
-  lo = __uint_as_float(f32_to_tf32_rna_int(v - hi));
+  lo = v - hi;
 }
 
 // 32 lanes x 16 consecutive 32-bit columns, load and store.

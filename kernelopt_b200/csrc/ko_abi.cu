@@ -77,6 +77,30 @@ int make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
   return KO_OK;
 }
 
+int make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t planes, uint64_t rows, uint64_t cols,
+                     uint64_t row_pitch_elems, uint64_t plane_pitch_elems, uint32_t box_rows, uint32_t box_cols,
+                     CUtensorMapSwizzle swizzle, const char* what) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(KO_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled is not available from the driver");
+  if (!aligned16(base) || (row_pitch_elems * 4) % 16 != 0 || (plane_pitch_elems * 4) % 16 != 0 ||
+      plane_pitch_elems == 0)
+    return fail(KO_ERR_INVALID_ARGUMENT, std::string(what) + ": base must be 16-byte aligned and the pitches "
+                                                             "non-zero multiples of 16 bytes");
+  cuuint64_t dims[3] = {cols, rows, planes};
+  cuuint64_t strides[2] = {row_pitch_elems * 4, plane_pitch_elems * 4};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[160];
+    snprintf(buf, sizeof buf, "%s: cuTensorMapEncodeTiled failed (CUresult %d)", what, static_cast<int>(r));
+    return fail(KO_ERR_INVALID_ARGUMENT, buf);
+  }
+  return KO_OK;
+}
+
 }  // namespace ko
 
 extern "C" {

@@ -149,7 +149,9 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q,
+                                                                        const __grid_constant__ CUtensorMap map_k,
+                                                                        const AttnArgs a) {
   using C = AttnCfg<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -166,6 +168,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
   uint64_t* mma_done = bars + 12;
   uint64_t* plo_free = bars + 13;  // P_j.V_j's P_lo products done (1 commit)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* q_tma = bars + 15;     // q tile landed (fp32) (1 arrival + tx bytes)
+  uint64_t* k0_tma = bars + 16;    // first k tile landed   (1 arrival + tx bytes)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -186,8 +190,20 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
     }
     mbar_init(mma_done, 1);
     mbar_init(plo_free, 1);
+    mbar_init(q_tma, 1);
+    mbar_init(k0_tma, 1);
     *abort_flag = 0;
     fence_barrier_init();
+    // The q tile and the first k tile come in by TMA at once (fp32, in the 128-byte-swizzled K-major layout the
+    // MMAs read, one 32-column box per 128-byte k-block); the loaders split them in place.
+    const int bq = a.q_bstride ? b : 0, bk = a.k_bstride ? b : 0;
+    mbar_arrive_expect_tx(q_tma, C::kQBytes);
+    mbar_arrive_expect_tx(k0_tma, C::kKBytes);
+#pragma unroll
+    for (int kb = 0; kb < C::kKB; ++kb) {
+      tma_load_3d(&map_q, q_tma, smem + kb * (BQ * 128), h * HD + kb * 32, q0, bq);
+      tma_load_3d(&map_k, k0_tma, smem + C::kOffKhi + kb * (BKEY * 128), h * HD + kb * 32, 0, bk);
+    }
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -402,35 +418,33 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
     }
   } else {
     // ---------------- loaders ----------------
-    // All 8 warps write the q tile; then warps 5-8 stream the k tiles and warps 9-12 the v tiles, each group
-    // holding its next tile in registers while the current one is in use.
+    // All 8 warps split the q tile (brought in by TMA) in place; warps 5-8 stream the k tiles and warps 9-12 the
+    // v tiles, each group holding its next tile in registers while the current one is in use. The first k tile
+    // also comes by TMA and is split in place by the k group.
     const int t = threadIdx.x - kLoadWarp0 * 32;  // 0..255
     constexpr int Q4 = HD / 4;                   // float4 per row
-    const float* qb = a.q + static_cast<int64_t>(b) * a.q_bstride + h * HD;
-    {
-      float4 reg[C::kQChunks];
-#pragma unroll
-      for (int i = 0; i < C::kQChunks; ++i) {
-        const int idx = i * kLoadThreads + t, r = idx / Q4, c = idx % Q4, tok = q0 + r;
-        reg[i] = tok < a.L ? __ldg(reinterpret_cast<const float4*>(qb + static_cast<int64_t>(tok) * a.q_row) + c)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int i = 0; i < C::kQChunks; ++i) {
-        const int idx = i * kLoadThreads + t, r = idx / Q4, c = idx % Q4;
-        const uint32_t off = (c >> 3) * (BQ * 128) + sw128(r, c & 7);
+    // hi in place, lo at the same offset in the lo buffer (the split is elementwise: any cover of the tile works)
+    auto split_in_place = [&](uint32_t off_hi, uint32_t off_lo, int n4, int tid, int nthreads) {
+      for (int i = tid; i < n4; i += nthreads) {
+        float4* src = reinterpret_cast<float4*>(smem + off_hi) + i;
+        const float4 v = *src;
         float4 hi, lo;
-        split_tf32(reg[i].x, hi.x, lo.x);
-        split_tf32(reg[i].y, hi.y, lo.y);
-        split_tf32(reg[i].z, hi.z, lo.z);
-        split_tf32(reg[i].w, hi.w, lo.w);
-        *reinterpret_cast<float4*>(smem + off) = hi;
-        *reinterpret_cast<float4*>(smem + C::kOffQlo + off) = lo;
+        split_tf32(v.x, hi.x, lo.x);
+        split_tf32(v.y, hi.y, lo.y);
+        split_tf32(v.z, hi.z, lo.z);
+        split_tf32(v.w, hi.w, lo.w);
+        *src = hi;
+        reinterpret_cast<float4*>(smem + off_lo)[i] = lo;
       }
       fence_proxy_async_smem();
       __syncwarp();
+    };
+    auto write_q = [&]() -> bool {
+      if (!mbar_wait(q_tma, 0, abort_flag)) return false;
+      split_in_place(0, C::kOffQlo, static_cast<int>(C::kQBytes / 16), t, kLoadThreads);
       if (lane == 0) mbar_arrive(q_ready);
-    }
+      return true;
+    };
     constexpr int kGroup = kLoadThreads / 2;       // 128 threads per group
     constexpr int kTileChunks = BKEY * HD / 4 / kGroup;
     const int g = t & (kGroup - 1);
@@ -446,8 +460,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
                             : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       };
-      load(0);
-      for (int j = 0; j < nkb; ++j) {
+      if (nkb > 1) load(1);
+      bool kok = write_q() && mbar_wait(k0_tma, 0, abort_flag);
+      if (kok) {
+        split_in_place(C::kOffKhi, C::kOffKlo, static_cast<int>(C::kKBytes / 16), g, kGroup);
+        if (lane == 0) mbar_arrive(k_full);
+      }
+      for (int j = 1; j < nkb && kok; ++j) {
         if (!mbar_wait(k_empty, (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag)) break;
 #pragma unroll
         for (int i = 0; i < kTileChunks; ++i) {
@@ -479,7 +498,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const Att
         }
       };
       load(0);
-      for (int j = 0; j < nkb; ++j) {
+      const bool vok = write_q();
+      for (int j = 0; j < nkb && vok; ++j) {
         if (!mbar_wait(v_empty, (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag)) break;
 #pragma unroll
         for (int i = 0; i < kTileChunks; ++i) {
@@ -554,6 +574,17 @@ extern "C" int ko_attention_f32(const float* q, const float* k, const float* v, 
   a.scale_log2 = scale * 1.4426950408889634f;
   a.dev_status = dev_status;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // q and k tiles by TMA: [batch][L][heads * head_dim] with the caller's strides, boxes of 32 columns x 128 rows
+  // (a stride of 0 between batch items maps every item to plane 0)
+  CUtensorMap mq, mk;
+  const uint64_t width = static_cast<uint64_t>(heads * head_dim);
+  int rc = ko::make_tmap_3d_f32(&mq, q, q_bstride ? batch : 1, L, width, q_row,
+                                q_bstride ? q_bstride : q_row * L + 4, BQ, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+                                "ko_attention_f32 q");
+  if (rc) return rc;
+  rc = ko::make_tmap_3d_f32(&mk, k, k_bstride ? batch : 1, L, width, k_row, k_bstride ? k_bstride : k_row * L + 4,
+                            BKEY, 32, CU_TENSOR_MAP_SWIZZLE_128B, "ko_attention_f32 k");
+  if (rc) return rc;
   dim3 grid(static_cast<unsigned>((L + BQ - 1) / BQ), static_cast<unsigned>(heads), static_cast<unsigned>(batch));
   const ko::DeviceInfo& info = ko::device_info();
   if (head_dim == 64) {
@@ -563,13 +594,13 @@ extern "C" int ko_attention_f32(const float* q, const float* k, const float* v, 
     cudaError_t e = cudaFuncSetAttribute(attention_tf32x3_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(C::kSmemBytes));
     if (e != cudaSuccess) return ko::fail(static_cast<int>(e), std::string(who) + ": cudaFuncSetAttribute failed");
-    attention_tf32x3_kernel<64><<<grid, kThreads, C::kSmemBytes, st>>>(a);
+    attention_tf32x3_kernel<64><<<grid, kThreads, C::kSmemBytes, st>>>(mq, mk, a);
   } else {
     using C = AttnCfg<32>;
     cudaError_t e = cudaFuncSetAttribute(attention_tf32x3_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(C::kSmemBytes));
     if (e != cudaSuccess) return ko::fail(static_cast<int>(e), std::string(who) + ": cudaFuncSetAttribute failed");
-    attention_tf32x3_kernel<32><<<grid, kThreads, C::kSmemBytes, st>>>(a);
+    attention_tf32x3_kernel<32><<<grid, kThreads, C::kSmemBytes, st>>>(mq, mk, a);
   }
   return ko::check_launch(who);
 }

@@ -36,6 +36,12 @@ EncodeTiledFn encode_tiled();
 int make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                      uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swizzle, const char* what);
 
+// 3-D fp32 tensor map over [planes][rows][cols] with row pitch `row_pitch_elems` and plane pitch
+// `plane_pitch_elems` (both in elements), box {box_cols, box_rows, 1}. Out-of-range elements read as zero.
+int make_tmap_3d_f32(CUtensorMap* map, const void* base, uint64_t planes, uint64_t rows, uint64_t cols,
+                     uint64_t row_pitch_elems, uint64_t plane_pitch_elems, uint32_t box_rows, uint32_t box_cols,
+                     CUtensorMapSwizzle swizzle, const char* what);
+
 }  // namespace ko
 
 // ---- device-side PTX wrappers -----------------------------------------------------------------------------
@@ -123,6 +129,16 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
           "r"(smem_addr(dst)),
       "l"(map), "r"(smem_addr(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// TMA: 3-D tiled load global -> shared, completion counted on an mbarrier (no cluster sharing).
+__device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int32_t c0, int32_t c1,
+                                            int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_addr(dst)),
+      "l"(map), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
 

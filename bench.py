@@ -34,13 +34,13 @@ WORKLOAD = ("RF-DETR-Medium fp32 inference on seeded 1920x1080 uint8 BGR frames:
             "projector + top-300 selection + 4-layer deformable decoder + heads, random-init weights (seed 0)")
 
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per GEMM launch, mean over the 95 GEMM launches of
-# one step, from one ncu capture of this benchmark at each batch size:
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per plain GEMM launch (gemm_tf32x3_kernel with the
+# bias / activation epilogue), mean over the 70 such launches of one step at 64 frames, from one ncu capture:
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --cache-control none
-#       --clock-control none -k regex:gemm_tf32x3 -c 95 python bench.py --batch B --steps 1 --warmup 3
-# 64 frames: 38 876 MB over the 95 launches (algorithmic bytes of the same launches: 38 916 MB);
-# 16 frames: 9 258 MB (algorithmic 9 905 MB).
-GEMM_TRAFFIC_PER_LAUNCH = {64: 409.2e6, 16: 97.45e6}
+#       --clock-control none -k regex:gemm_tf32x3 -c 95 python bench.py --steps 1 --warmup 3 --no-cpu-baseline
+# (the first 95 launches matching the pattern are the step's 70 plain and 25 LayerNorm-epilogue GEMMs; the plain
+# ones total 34 076 MB against 33 864 MB of algorithmic bytes: x, the output and the split weight once each).
+GEMM_TRAFFIC_PER_LAUNCH = {64: 486.8e6}
 
 
 def frames_for(rank: int, n: int) -> np.ndarray:

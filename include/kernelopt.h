@@ -179,6 +179,20 @@ int ko_linear_gelu_f32(const float* x, const float* w, const float* bias, int64_
 int ko_linear_gelu_f32_noalloc(const float* x, const float* w, const float* bias, int64_t M, int64_t K, int64_t N,
                                float* out, int* dev_status, ko_stream_t stream);
 
+/* --- query selection ------------------------------------------------------------------------------------------ */
+
+/* The top-NQ proposals of each frame by class score, and their refined reference boxes:
+ *   score[b, i] = max_c logits[b, i, c];   order = proposals by descending score, ties by ascending index
+ *   c = coord(b, idx[b, q]) with coord = (delta_xy * prop_wh + prop_xy, exp(delta_wh) * prop_wh)
+ *   ref[b, q] = (rp_xy[q] * c_wh + c_xy, rp_ewh[q] * c_wh)
+ * logits: float32 [B][NP][NC]; delta: float32 [B][NP][4]; proposals: float32 [NP][4] (cx, cy, w, h);
+ * rp_xy, rp_ewh: float32 [NQ][2]; ref: float32 [B][NQ][4]; idx: int32 [B][NQ] or NULL. 1 <= NQ <= NP <= 4096.
+ * delta, proposals and ref 16-byte aligned, rp_xy and rp_ewh 8-byte aligned. Replaces select_queries'
+ * max / argsort / take_along_axis / box refinement (fast_rfdetr/model.py:175-185). */
+int ko_select_queries(const float* logits, const float* delta, const float* proposals, const float* rp_xy,
+                      const float* rp_ewh, int64_t B, int64_t NP, int64_t NC, int64_t NQ, float* ref, int32_t* idx,
+                      ko_stream_t stream);
+
 /* --- multi-head attention, fp32 grade (3xTF32 on tcgen05, flash style) ------------------------------------- */
 
 /* o[b, i, h, :] = sum_j softmax_j(scale * q[b, i, h, :] . k[b, j, h, :]) v[b, j, h, :], no mask.

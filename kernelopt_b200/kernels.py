@@ -257,6 +257,28 @@ def linear(x, pw: PackedWeight, act=None, out=None):
     return out
 
 
+def select_queries(logits, delta, proposals, rp_xy, rp_ewh, nq, ref=None, idx=None):
+    """The reference's query selection (model.py:175-185) in one kernel: per frame the nq proposals with the
+    highest class score (max over the last dimension of logits; ties by ascending index), and their reference
+    boxes refined with rp_xy / rp_ewh. logits [B, NP, NC], delta [B, NP, 4], proposals [NP, 4], rp_xy and
+    rp_ewh [nq, 2]. Returns (ref [B, nq, 4], idx [B, nq] int32)."""
+    for name, t in (("logits", logits), ("delta", delta), ("proposals", proposals), ("rp_xy", rp_xy),
+                    ("rp_ewh", rp_ewh)):
+        _need(t, name)
+    b, n_p, n_c = logits.shape
+    if tuple(delta.shape) != (b, n_p, 4) or tuple(proposals.shape) != (n_p, 4):
+        raise ValueError("delta must be [B, NP, 4] and proposals [NP, 4]")
+    if tuple(rp_xy.shape) != (nq, 2) or tuple(rp_ewh.shape) != (nq, 2):
+        raise ValueError("rp_xy and rp_ewh must be [nq, 2]")
+    if ref is None:
+        ref = torch.empty((b, nq, 4), dtype=torch.float32, device=logits.device)
+    if idx is None:
+        idx = torch.empty((b, nq), dtype=torch.int32, device=logits.device)
+    call("ko_select_queries", logits.data_ptr(), delta.data_ptr(), proposals.data_ptr(), rp_xy.data_ptr(),
+         rp_ewh.data_ptr(), b, n_p, n_c, nq, ref.data_ptr(), idx.data_ptr(), _stream())
+    return ref, idx
+
+
 LN_WIDTHS = (128, 192, 256, 384, 512)
 
 

@@ -13,8 +13,8 @@ the decoder linears) runs on the same fp32-grade tcgen05 GEMM; only the layers w
 multiple of 4 (11 classes, 4 box coordinates) use torch's fp32 matmul. Attention — the backbone's windowed and
 global self-attention and the decoder's self-attention (the reference's mx.fast.scaled_dot_product_attention) — runs
 on the fp32-grade 3xTF32 tcgen05 flash-attention kernel, straight on column slices of the fused QKV projection.
-The remaining LayerNorms run on the LayerNorm kernel; softmax and top-300 are torch ops in fp32 with TF32
-disabled.
+The remaining LayerNorms run on the LayerNorm kernel; the top-300 query selection is one kernel; softmax is a torch
+op in fp32 with TF32 disabled.
 
 The input is the patch layout the preprocessing kernel writes (PATCH16: [B, 1600, 768]), which makes the
 16x16/16 patch-embedding convolution one GEMM; NHWC [B, 640, 640, 3] (the reference's input) is accepted too.
@@ -236,18 +236,17 @@ class RFDETR:
         x = layers[1](x, "relu")
         return layers[2](x)
 
-    def select_queries(self, memory):
-        """model.py:175-185: class score per proposal, box refinement, top-300 by score."""
+    def select_queries(self, memory, with_scores=True):
+        """model.py:175-185: class score per proposal, box refinement, top-300 by score. The score maximum, the
+        ranking (ties by ascending proposal index), the gather and the box refinement are one kernel
+        (ko_select_queries). Returns (ref [B, 300, 4], scores [B, 1600] or None, idx [B, 300])."""
         om = memory * self.valid
         _, om = self.enc_output.ln(om, self.enc_norm)
-        scores = self.enc_class(om).amax(-1)                                                    # [B, 1600]
-        delta = self._mlp3(om, self.enc_bbox)
-        prop = self.props
-        coord = torch.cat([delta[..., :2] * prop[:, 2:] + prop[:, :2], torch.exp(delta[..., 2:]) * prop[:, 2:]], -1)
-        idx = torch.topk(scores, N_QUERIES, dim=-1, largest=True, sorted=True).indices
-        ts = torch.gather(coord, 1, idx[..., None].expand(-1, -1, 4))
-        ref = torch.cat([self.rp_xy * ts[..., 2:] + ts[..., :2], self.rp_ewh * ts[..., 2:]], -1)
-        return ref, scores, idx
+        logits = self.enc_class(om)                                                             # [B, 1600, 11]
+        delta = self._mlp3(om, self.enc_bbox)                                                   # [B, 1600, 4]
+        ref, idx = K.select_queries(logits.contiguous(), delta.contiguous(), self.props, self.rp_xy, self.rp_ewh,
+                                    N_QUERIES)
+        return ref, (logits.amax(-1) if with_scores else None), idx
 
     # ---- decoder ----------------------------------------------------------------------------------------------
     def sine_embed(self, ref):
@@ -289,7 +288,7 @@ class RFDETR:
         b = x.shape[0]
         feats = self.backbone(x)
         memory = self.projector(feats).reshape(b, GRID * GRID, D_MODEL)
-        ref, _, _ = self.select_queries(memory)
+        ref, _, _ = self.select_queries(memory, with_scores=False)
         hs = self.decoder(memory, ref)
         logits = self.class_embed(hs)
         delta = self._mlp3(hs, self.bbox_embed)

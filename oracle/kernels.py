@@ -88,3 +88,18 @@ def deform_attn(value, loc, aw, grid_hw, nh, hd, offset=0):
             g = v[bi, tok, hi]                                                      # [B, NQ, NH, NP, HD]
             out += g * np.where(ok, wx * wy, 0.0)[..., None]
     return (out * aw[..., None]).sum(axis=3).reshape(b, nq, nh * hd)
+
+
+def select_queries(logits, delta, proposals, rp_xy, rp_ewh, nq):
+    """model.py:175-185 after the two heads: score = max over classes, coord = refined proposal, the nq best
+    proposals by a stable descending sort (ties by ascending index), ref = the selected coords refined by the
+    query reference points. Returns (ref [B, nq, 4] float64, idx [B, nq])."""
+    logits = np.asarray(logits, np.float64)
+    delta = np.asarray(delta, np.float64)
+    prop = np.asarray(proposals, np.float64)
+    scores = logits.max(-1)
+    coord = np.concatenate([delta[..., :2] * prop[:, 2:] + prop[:, :2], np.exp(delta[..., 2:]) * prop[:, 2:]], -1)
+    idx = np.argsort(-np.asarray(logits, np.float32).max(-1), axis=-1, kind="stable")[:, :nq]
+    ts = np.take_along_axis(coord, idx[..., None], axis=1)
+    rxy, rwh = np.asarray(rp_xy, np.float64), np.asarray(rp_ewh, np.float64)
+    return np.concatenate([rxy * ts[..., 2:] + ts[..., :2], rwh * ts[..., 2:]], -1), idx

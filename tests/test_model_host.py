@@ -62,6 +62,14 @@ def _lrln(x, pw, gamma, beta, eps, resid=None, scale=None, act=None, h_out=None,
     return (ho if write_h else None), (F.silu(yy) if act == "silu" else yy)
 
 
+def _select(logits, delta, prop, rp_xy, rp_ewh, nq, ref=None, idx=None):
+    scores = logits.amax(-1)
+    coord = torch.cat([delta[..., :2] * prop[:, 2:] + prop[:, :2], torch.exp(delta[..., 2:]) * prop[:, 2:]], -1)
+    i = torch.from_numpy(np.argsort(-scores.numpy(), axis=-1, kind="stable")[:, :nq].copy())
+    ts = torch.gather(coord, 1, i[..., None].expand(-1, -1, 4))
+    return torch.cat([rp_xy * ts[..., 2:] + ts[..., :2], rp_ewh * ts[..., 2:]], -1), i
+
+
 def _im2col3x3(x, out=None):
     b, h, w, c = x.shape
     xp = F.pad(x, (0, 0, 1, 1, 1, 1))
@@ -80,6 +88,7 @@ def cpu_model(monkeypatch):
     monkeypatch.setattr(K, "layernorm", _layernorm)
     monkeypatch.setattr(K, "im2col3x3", _im2col3x3)
     monkeypatch.setattr(K, "linear_residual_layernorm", _lrln)
+    monkeypatch.setattr(K, "select_queries", _select)
     monkeypatch.setattr(K, "status_word", lambda *a: None)
     w = random_weights(0)
 

@@ -179,6 +179,18 @@ int ko_linear_gelu_f32(const float* x, const float* w, const float* bias, int64_
 int ko_linear_gelu_f32_noalloc(const float* x, const float* w, const float* bias, int64_t M, int64_t K, int64_t N,
                                float* out, int* dev_status, ko_stream_t stream);
 
+/* A 3x3 convolution (stride 1, zero padding 1) as an implicit GEMM on the same tensor cores, with the LayerNorm
+ * (+ SiLU) of ko_linear_residual_ln_f32_packed in its epilogue and no residual:
+ *   y[p] = act(LN(sum_{ky,kx,c} x[b][py+ky-1][px+kx-1][c] * w[(ky*3+kx)*C + c][:] + bias) * gamma + beta)
+ * x: float32 NHWC [B][H][W][C], C % 16 == 0; w_packed: ko_pack_weight_tf32x3 of the weight as [9*C][N] in
+ * (ky, kx, c) row order (the conv weight [N][3][3][C] flattened and transposed); y: float32 [B*H*W][N]; N one of
+ * 128, 192, 256, 384, 512. No im2col buffer: each k-block's TMA load reads x shifted by the tap, and rows whose
+ * shifted pixel lies outside the image are zeroed on chip. Replaces the projector's conv -> channel LayerNorm ->
+ * SiLU blocks (fast_rfdetr/model.py:148-158) with one kernel each. */
+int ko_conv3x3_ln_f32_packed(const float* x, const float* w_packed, const float* bias, const float* gamma,
+                             const float* beta, float eps, int64_t B, int64_t H, int64_t W, int64_t C, int64_t N,
+                             int act, float* y, int* dev_status, ko_stream_t stream);
+
 /* --- query selection ------------------------------------------------------------------------------------------ */
 
 /* The top-NQ proposals of each frame by class score, and their refined reference boxes:

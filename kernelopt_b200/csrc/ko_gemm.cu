@@ -95,6 +95,11 @@ struct GemmArgs {
   float eps;
   int write_v;  // store v = resid + (acc + bias) * scale through map_v
   int cs;       // CTAs per cluster = N / BN
+  // Implicit 3x3 convolution (stride 1, zero padding 1) when conv_c > 0: x is an NHWC image batch
+  // [M = batch * conv_h * conv_w][conv_c], K = 9 * conv_c in (ky, kx, c) order, and k-block kb reads the rows of
+  // x shifted by (ky - 1) * conv_w + (kx - 1) for tap ky * 3 + kx; rows whose shifted pixel lies outside the
+  // image are zeroed by the split warps.
+  int conv_h, conv_w, conv_c;
 };
 
 // Tiles of one CTA. EPI_ACT: tile t of the m_tiles x n_tiles grid, CTAs strided over tiles. EPI_LN: tile t is
@@ -249,7 +254,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sbase = smem + st * C::kStageBytes;
           mbar_arrive_expect_tx(&full[st], C::kTxBytes);
-          tma_load_2d(&map_x, &full[st], sbase, kb * C::kBK, m0);
+          if (args.conv_c > 0) {
+            const int cpb = args.conv_c / C::kBK;  // k-blocks per tap
+            const int tap = kb / cpb;
+            tma_load_2d(&map_x, &full[st], sbase, (kb - tap * cpb) * C::kBK,
+                        m0 + (tap / 3 - 1) * args.conv_w + (tap % 3 - 1));
+          } else {
+            tma_load_2d(&map_x, &full[st], sbase, kb * C::kBK, m0);
+          }
           tma_load_2d(&map_whi, &full[st], sbase + 2 * C::kATileBytes, kb * C::kBK, n0);
           tma_load_2d(&map_wlo, &full[st], sbase + 2 * C::kATileBytes + C::kBTileBytes, kb * C::kBK, n0);
 #pragma unroll
@@ -326,23 +338,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     // split at once and each group has two MMA k-blocks of time per stage.
     const int group = (warp - kTransformWarp0) >> 2;
     const int t = (threadIdx.x - kTransformWarp0 * 32) & 127;  // 0..127 within the group
+    constexpr int kPer = static_cast<int>(C::kATileBytes / 16 / 128);  // float4 of the tile per thread
+    constexpr int kRowF4 = BKB / 16;                                    // float4 per tile row
+    const bool conv = args.conv_c > 0;
     int st = 0;
     uint32_t phase = 0;
     uint32_t it = 0;
     bool ok = true;
     for (int tile = ts.first; tile < num_tiles && ok; tile += ts.step) {
+      // implicit convolution: image coordinates of the rows this thread splits (fixed for the tile)
+      int py[kPer], px[kPer];
+      if (conv) {
+        const int m0 = ts.m0(tile), hw = args.conv_h * args.conv_w;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int rem = (m0 + (t + i * 128) / kRowF4) % hw;
+          py[i] = rem / args.conv_w;
+          px[i] = rem - py[i] * args.conv_w;
+        }
+      }
       for (int kb = 0; kb < args.k_blocks; ++kb, ++it) {
         if ((it & 1u) == static_cast<uint32_t>(group)) {
           if (!mbar_wait(&full[st], phase, abort_flag)) {
             ok = false;
             break;
           }
+          int dy = 0, dx = 0;
+          if (conv) {
+            const int tap = kb / (args.conv_c / C::kBK);
+            dy = tap / 3 - 1;
+            dx = tap % 3 - 1;
+          }
           float4* xa = reinterpret_cast<float4*>(smem + st * C::kStageBytes);
           float4* xl = reinterpret_cast<float4*>(smem + st * C::kStageBytes + C::kATileBytes);
 #pragma unroll
-          for (int i = 0; i < static_cast<int>(C::kATileBytes / 16 / 128); ++i) {
+          for (int i = 0; i < kPer; ++i) {
             const int idx = t + i * 128;
-            const float4 v = xa[idx];
+            float4 v = xa[idx];
+            if (conv) {
+              const int yy = py[i] + dy, xx = px[i] + dx;
+              if (yy < 0 || yy >= args.conv_h || xx < 0 || xx >= args.conv_w) v = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
             float4 hi, lo;
             hi.x = __uint_as_float(f32_to_tf32_rna(v.x));
             hi.y = __uint_as_float(f32_to_tf32_rna(v.y));
@@ -724,13 +760,15 @@ int launch_gemm(const float* x, const float* w_packed, const float* bias, int64_
 template <int BN, bool SPLIT>
 int launch_gemm_ln(const float* x, const float* w_packed, const float* bias, const float* scale, const float* resid,
                    const float* gamma, const float* beta, float eps, int64_t M, int64_t K, int64_t N, int act,
-                   float* v_out, float* y, int* dev_status, cudaStream_t stream) {
+                   float* v_out, float* y, int* dev_status, cudaStream_t stream, int conv_h = 0, int conv_w = 0,
+                   int conv_c = 0) {
   constexpr int BKB = 64;
   using C = Cfg<BN, BKB, SPLIT, EPI_LN>;
   const int cs = static_cast<int>(N / BN);
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_64B;
   CUtensorMap mx, mhi, mlo, my, mv;
-  int st = ko::make_tmap_2d_f32(&mx, x, M, K, K, BM, C::kBK, sw, "ko_linear_residual_ln x");
+  const int64_t xcols = conv_c > 0 ? conv_c : K;  // an implicit convolution reads x as [M][C]
+  int st = ko::make_tmap_2d_f32(&mx, x, M, xcols, xcols, BM, C::kBK, sw, "ko_linear_residual_ln x");
   if (st) return st;
   st = ko::make_tmap_2d_f32(&mhi, w_packed, N, K, K, BN, C::kBK, sw, "ko_linear_residual_ln w_hi");
   if (st) return st;
@@ -770,6 +808,9 @@ int launch_gemm_ln(const float* x, const float* w_packed, const float* bias, con
   a.eps = eps;
   a.write_v = v_out != nullptr;
   a.cs = cs;
+  a.conv_h = conv_h;
+  a.conv_w = conv_w;
+  a.conv_c = conv_c;
 
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -936,6 +977,39 @@ extern "C" int ko_linear_residual_ln_f32_packed(const float* x, const float* w_p
   KO_LN_CASE(192)
   KO_LN_CASE(256)
 #undef KO_LN_CASE
+  return ko::fail(KO_ERR_UNSUPPORTED, std::string(who) + ": no tile for this N");
+}
+
+extern "C" int ko_conv3x3_ln_f32_packed(const float* x, const float* w_packed, const float* bias, const float* gamma,
+                                        const float* beta, float eps, int64_t B, int64_t H, int64_t W, int64_t C,
+                                        int64_t N, int act, float* y, int* dev_status, ko_stream_t stream) {
+  const char* who = "ko_conv3x3_ln_f32_packed";
+  if (B < 0 || H < 1 || W < 1 || C < 16 || C % 16 != 0 || B * H * W > INT32_MAX || C > 4096)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": need C % 16 == 0 and a batch below 2^31 pixels");
+  const int64_t M = B * H * W, K = 9 * C;
+  int st = validate_linear(x, w_packed, bias, M, K, N, y, who);
+  if (st || M == 0) return st;
+  if (N != 128 && N != 192 && N != 256 && N != 384 && N != 512)
+    return ko::fail(KO_ERR_UNSUPPORTED, std::string(who) + ": N must be 128, 192, 256, 384 or 512");
+  if (act != KO_ACT_NONE && act != KO_ACT_SILU)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": act must be KO_ACT_NONE or KO_ACT_SILU");
+  if (!gamma || !beta || !(eps >= 0.0f) || !ko::aligned16(gamma) || !ko::aligned16(beta))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": gamma, beta required and 16-byte aligned; eps >= 0");
+  if (y == x) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": y must not alias x");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool split = K > 512;
+  const int bn = N == 384 ? 192 : N == 512 ? 256 : static_cast<int>(N);
+  const int h = static_cast<int>(H), w = static_cast<int>(W), c = static_cast<int>(C);
+#define KO_CONV_CASE(BNV)                                                                                        \
+  if (bn == BNV)                                                                                                \
+    return split ? launch_gemm_ln<BNV, true>(x, w_packed, bias, nullptr, nullptr, gamma, beta, eps, M, K, N, act, \
+                                             nullptr, y, dev_status, s, h, w, c)                                  \
+                 : launch_gemm_ln<BNV, false>(x, w_packed, bias, nullptr, nullptr, gamma, beta, eps, M, K, N, act,\
+                                              nullptr, y, dev_status, s, h, w, c);
+  KO_CONV_CASE(128)
+  KO_CONV_CASE(192)
+  KO_CONV_CASE(256)
+#undef KO_CONV_CASE
   return ko::fail(KO_ERR_UNSUPPORTED, std::string(who) + ": no tile for this N");
 }
 

@@ -316,6 +316,32 @@ def linear_residual_layernorm(x, pw: PackedWeight, gamma, beta, eps, resid=None,
     return (h_out if write_h else None), y
 
 
+def conv3x3_layernorm(x, pw: PackedWeight, gamma, beta, eps, act=None, out=None):
+    """act(LayerNorm(conv3x3(x) + bias) * gamma + beta) for an NHWC float32 x [B, H, W, C] (C % 16 == 0): the
+    3x3 / stride 1 / padding 1 convolution as an implicit GEMM (no im2col buffer) with the LayerNorm epilogue.
+    pw: the weight as [9*C, N] in (ky, kx, c) row order (PackedWeight; its bias is the conv bias). Returns
+    [B*H*W, N]. The projector's conv -> channel LayerNorm -> SiLU block (model.py:148-158) in one kernel."""
+    _need(x, "x")
+    if x.dim() != 4:
+        raise ValueError("x must be [B, H, W, C]")
+    b, h, w, c = x.shape
+    if pw.k != 9 * c:
+        raise ValueError(f"the weight has {pw.k} rows, a 3x3 convolution over {c} channels needs {9 * c}")
+    if pw.n not in LN_WIDTHS:
+        raise ValueError(f"output width {pw.n} is not one of {LN_WIDTHS}")
+    for name, t in (("gamma", gamma), ("beta", beta)):
+        if _need(t, name).numel() != pw.n:
+            raise ValueError(f"{name} must have {pw.n} elements")
+    if act not in (None, "none", "silu"):
+        raise ValueError("act must be None or 'silu'")
+    if out is None:
+        out = torch.empty((b * h * w, pw.n), dtype=torch.float32, device=x.device)
+    call("ko_conv3x3_ln_f32_packed", x.data_ptr(), pw.packed.data_ptr(), _ptr(pw.bias), gamma.data_ptr(),
+         beta.data_ptr(), float(eps), b, h, w, c, pw.n, _lib.KO_ACT_SILU if act == "silu" else _lib.KO_ACT_NONE,
+         out.data_ptr(), status_word(x.device).data_ptr(), _stream())
+    return out
+
+
 _pack_cache: "weakref.WeakKeyDictionary[torch.Tensor, tuple[int, PackedWeight]]" = weakref.WeakKeyDictionary()
 _pack_lock = threading.Lock()
 

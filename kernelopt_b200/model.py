@@ -215,11 +215,15 @@ class RFDETR:
     def _convx(self, x, cv):
         """conv (as GEMM; 3x3 through im2col) + channel LayerNorm + SiLU (model.py:148-158)."""
         b, hh, ww, cin = x.shape
+        dense = cv["dense"]
         if cv["k"] == 1:
             cols = x.reshape(b * hh * ww, cin)
+        elif dense.native and dense.n in K.LN_WIDTHS and cin % 16 == 0:
+            w, bt, eps = cv["ln"]                                  # implicit-GEMM conv + LN + SiLU, one kernel
+            return K.conv3x3_layernorm(x.contiguous(), dense.pw, w, bt, eps, "silu").reshape(b, hh, ww, -1)
         else:
             cols = K.im2col3x3(x.contiguous())                                                   # [B*H*W, 9*cin]
-        _, y = cv["dense"].ln(cols, cv["ln"], act="silu")                                     # GEMM + LN + SiLU
+        _, y = dense.ln(cols, cv["ln"], act="silu")                                           # GEMM + LN + SiLU
         return y.reshape(b, hh, ww, -1)
 
     def projector(self, feats):

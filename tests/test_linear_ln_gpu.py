@@ -120,3 +120,40 @@ def test_empty_rows(cuda):
     x = torch.empty((0, 384), device=cuda)
     h, y = K.linear_residual_layernorm(x, pw, t(d["gamma"]), t(d["beta"]), 1e-6)
     assert h.shape == (0, 384) and y.shape == (0, 384)
+
+
+def im2col3x3_np(x):
+    b, h, w, c = x.shape
+    xp = np.pad(x, ((0, 0), (1, 1), (1, 1), (0, 0)))
+    return np.concatenate([xp[:, dy:dy + h, dx:dx + w] for dy in range(3) for dx in range(3)], -1).reshape(
+        b * h * w, 9 * c)
+
+
+@pytest.mark.parametrize("b,h,w,c,n", [(2, 40, 40, 128, 128), (1, 7, 5, 16, 128), (3, 40, 40, 128, 256),
+                                       (1, 1, 1, 32, 128), (2, 9, 13, 48, 384)])
+def test_conv3x3_ln_silu(cuda, b, h, w, c, n):
+    """Implicit-GEMM 3x3 convolution + LayerNorm + SiLU against im2col + GEMM + LN + SiLU in float64."""
+    r = np.random.default_rng(b * 1000 + h * 10 + c)
+    x = r.standard_normal((b, h, w, c)).astype(np.float32)
+    wt = (r.standard_normal((9 * c, n)) / np.sqrt(9 * c)).astype(np.float32)
+    bias = (0.1 * r.standard_normal(n)).astype(np.float32)
+    gamma = (1.0 + 0.1 * r.standard_normal(n)).astype(np.float32)
+    beta = (0.1 * r.standard_normal(n)).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    pw = K.pack_weight(t(wt), t(bias))
+    y = K.conv3x3_layernorm(t(x), pw, t(gamma), t(beta), 1e-6, act="silu")
+    torch.cuda.synchronize()
+    K.check_device_status()
+    _, ry = OK.linear_residual_layernorm(im2col3x3_np(x), wt, bias, None, None, gamma, beta, 1e-6, "silu")
+    assert_close(y, ry, what=f"conv {b}x{h}x{w}x{c}->{n}")
+    # the same values as the explicit im2col path
+    _, y2 = K.linear_residual_layernorm(K.im2col3x3(t(x)), pw, t(gamma), t(beta), 1e-6, act="silu", write_h=False)
+    torch.cuda.synchronize()
+    assert (y - y2).abs().max().item() <= 1e-5 * y2.abs().max().item()
+
+
+def test_conv3x3_rejects_bad_channels(cuda):
+    x = torch.zeros((1, 4, 4, 20), device=cuda)
+    pw = K.pack_weight(torch.zeros((180, 128), device=cuda))
+    with pytest.raises(ValueError):
+        K.conv3x3_layernorm(x, pw, torch.ones(128, device=cuda), torch.zeros(128, device=cuda), 1e-6)

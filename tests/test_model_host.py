@@ -70,6 +70,10 @@ def _select(logits, delta, prop, rp_xy, rp_ewh, nq, ref=None, idx=None):
     return torch.cat([rp_xy * ts[..., 2:] + ts[..., :2], rp_ewh * ts[..., 2:]], -1), i
 
 
+def _conv3x3_ln(x, pw, gamma, beta, eps, act=None, out=None):
+    return _lrln(_im2col3x3(x), pw, gamma, beta, eps, act=act, write_h=False)[1]
+
+
 def _im2col3x3(x, out=None):
     b, h, w, c = x.shape
     xp = F.pad(x, (0, 0, 1, 1, 1, 1))
@@ -89,6 +93,7 @@ def cpu_model(monkeypatch):
     monkeypatch.setattr(K, "im2col3x3", _im2col3x3)
     monkeypatch.setattr(K, "linear_residual_layernorm", _lrln)
     monkeypatch.setattr(K, "select_queries", _select)
+    monkeypatch.setattr(K, "conv3x3_layernorm", _conv3x3_ln)
     monkeypatch.setattr(K, "status_word", lambda *a: None)
     w = random_weights(0)
 

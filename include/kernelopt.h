@@ -58,6 +58,11 @@ const char* ko_last_error_string(void);
 int ko_abi_version(void);
 /* 0 when the current device is an sm_100-class GPU this library was built for, else KO_ERR_UNSUPPORTED. */
 int ko_check_device(void);
+/* Runs the bounded on-chip wait of the tcgen05 kernels on a barrier that nothing completes: after limit_ns the
+ * wait gives up, a second warp waiting on the same barrier leaves on the CTA's abort flag, and
+ * KO_ERR_DEVICE_TIMEOUT is written to *dev_status (device memory) — the failure path of every kernel with
+ * on-chip waits, without a fault. For tests and health checks; no counterpart in the reference. */
+int ko_wait_probe(int64_t limit_ns, int* dev_status, ko_stream_t stream);
 
 /* --- preprocessing: uint8 BGR frame -> resized, RGB, normalised float32 ------------------------------------ */
 

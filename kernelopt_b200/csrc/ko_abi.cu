@@ -118,3 +118,36 @@ int ko_check_device(void) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------------------
+// ko_wait_probe: the bounded on-chip wait of the tcgen05 kernels, run on an mbarrier that nothing arrives on.
+// Warp 0 waits (mbar_wait_for, the code path behind every mbar_wait) until limit_ns pass and raises the CTA's
+// abort flag; warp 1 waits on the same barrier with the full limit and must leave as soon as it sees the flag;
+// thread 0 then writes KO_ERR_DEVICE_TIMEOUT to *dev_status, as the kernels do. Nothing faults and the
+// context stays usable: this is how the timeout path is exercised in tests.
+// ---------------------------------------------------------------------------------------------------------
+namespace {
+__global__ void wait_probe_kernel(uint64_t limit_ns, int* dev_status) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    kodev::mbar_init(&bar, 1);
+    abort_flag = 0;
+    kodev::fence_barrier_init();
+  }
+  __syncthreads();
+  volatile int* abort = &abort_flag;
+  bool ok = true;
+  if (threadIdx.x < 32) ok = kodev::mbar_wait_for(&bar, 0, abort, limit_ns);
+  else ok = kodev::mbar_wait(&bar, 0, abort);
+  __syncthreads();
+  if (threadIdx.x == 0 && (!ok || *abort) && dev_status) atomicExch(dev_status, KO_ERR_DEVICE_TIMEOUT);
+}
+}  // namespace
+
+extern "C" int ko_wait_probe(int64_t limit_ns, int* dev_status, ko_stream_t stream) {
+  if (limit_ns < 0 || limit_ns > 10000000000ll || !dev_status)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_wait_probe: need 0 <= limit_ns <= 10 s and a status word");
+  wait_probe_kernel<<<1, 64, 0, reinterpret_cast<cudaStream_t>(stream)>>>(static_cast<uint64_t>(limit_ns), dev_status);
+  return ko::check_launch("ko_wait_probe");
+}

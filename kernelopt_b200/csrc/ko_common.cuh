@@ -91,21 +91,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Wall-clock bound of every on-chip wait (nanoseconds). A healthy wait ends within microseconds.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-// Bounded wait for the phase with `parity` to complete. Returns false (and raises *abort) if the wait runs out
-// or another role of the CTA already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// Bounded wait for the phase with `parity` to complete within `limit_ns`. Returns false (and raises *abort) if
+// the wait runs out or another role of the CTA already aborted.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t start = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 31u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - start > kWaitLimitNs) {
+      if (globaltimer_ns() - start > limit_ns) {
         *abort = 1;
         return false;
       }
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  return mbar_wait_for(bar, parity, abort, kWaitLimitNs);
 }
 
 // mbar_wait whose result is the same in every lane of the warp (for warp-uniform loops).

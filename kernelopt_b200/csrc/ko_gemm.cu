@@ -15,8 +15,10 @@
 // Kernel structure (persistent, one CTA per SM, 576 threads, warp-specialised):
 //   warp 0      TMA producer: x tile [128 x BK] and W_hi/W_lo tiles [BN x BK] per k-block, swizzled
 //   warp 1      allocates TMEM; one lane issues the tcgen05.mma (3 products per 8-wide k-step)
-//   warps 2-9   split the x tile in shared memory: hi in place, lo into a second buffer (same layout); two
-//               groups of four warps take alternate k-blocks
+//   warps 2-9   split the x tile: hi in place and lo into a second buffer (same layout) in shared memory, or,
+//               for 192-wide tiles, hi and lo into the stage's slot of tensor memory, where the MMA reads A
+//               (the "TS" form; only B then comes from shared memory); two groups of four warps take
+//               alternate k-blocks
 //   warps 10-17 epilogue: TMEM -> registers (tcgen05.ld), + bias, activation, a swizzled 32x32 tile in shared
 //               memory per warp, TMA store (two warps per TMEM lane quadrant)
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the MMAs of tile i+1.
@@ -64,13 +66,19 @@ struct Cfg {
   static constexpr int kBK = BKB / 4;                       // fp32 elements per k-block
   static constexpr uint32_t kATileBytes = BM * BKB;
   static constexpr uint32_t kBTileBytes = BN * BKB;
-  static constexpr uint32_t kStageBytes = 2 * kATileBytes + 2 * kBTileBytes;
+  // A from tensor memory (the split warps write x_hi / x_lo into a TMEM slot per stage, the MMA reads A there
+  // and only B from shared memory) for 192-wide tiles, where the accumulators leave 128 TMEM columns free.
+  static constexpr bool kTSA = BN == 192 && BKB == 64;
+  static constexpr uint32_t kStageBytes = (kTSA ? 1 : 2) * kATileBytes + 2 * kBTileBytes;
   static constexpr uint32_t kStatBytes = EPI == EPI_LN ? kLnStatRegion : 0;
   static constexpr int kStagesRaw = static_cast<int>((kSmemBudget - kStatBytes) / kStageBytes);
-  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static constexpr int kStages = kTSA ? (kStagesRaw > 4 ? 4 : kStagesRaw) : (kStagesRaw > 8 ? 8 : kStagesRaw);
+  static constexpr uint32_t kASlotCols = 2 * kBK;                    // A_hi | A_lo of one k-block in TMEM
+  static constexpr uint32_t kATmemCols = kTSA ? kStages * kASlotCols : 0;
   static constexpr uint32_t kAccCols = BN * (SPLIT ? 2 : 1);  // TMEM columns of one tile's accumulator(s)
-  static constexpr int kAccBufs = (2 * kAccCols <= 512) ? 2 : 1;
-  static constexpr uint32_t kTmemNeed = kAccBufs * kAccCols;
+  static constexpr int kAccBufs = (2 * kAccCols + kATmemCols <= 512) ? 2 : 1;
+  static constexpr uint32_t kAOffCol = kAccBufs * kAccCols;  // first TMEM column of the A slots
+  static constexpr uint32_t kTmemNeed = kAccBufs * kAccCols + kATmemCols;
   static constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
                                         : kTmemNeed <= 256 ? 256 : 512;
   static constexpr uint32_t kTxBytes = kATileBytes + 2 * kBTileBytes;
@@ -78,7 +86,7 @@ struct Cfg {
   static constexpr uint32_t kSbo = 8 * BKB;                 // bytes between 8-row groups
   static constexpr uint32_t kLayout = BKB == 128 ? 2u : 4u;  // descriptor layout: 128B / 64B swizzle
   static_assert(kStages >= 2, "stage does not fit");
-  static_assert(kAccCols * kAccBufs <= 512, "TMEM overflow");
+  static_assert(kTmemNeed <= 512, "TMEM overflow");
 };
 
 struct GemmArgs {
@@ -153,6 +161,14 @@ __device__ __forceinline__ void tmem_store_x32(uint32_t taddr, const uint32_t (&
       : "memory");
 }
 __device__ __forceinline__ void tmem_store_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_store_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 
 // (mean, M2) of two equal-sized groups of n values each, combined in the order (a, b) (Chan et al., 1979).
 __device__ __forceinline__ float2 combine_stats(float2 a, float2 b, float n) {
@@ -262,8 +278,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             tma_load_2d(&map_x, &full[st], sbase, kb * C::kBK, m0);
           }
-          tma_load_2d(&map_whi, &full[st], sbase + 2 * C::kATileBytes, kb * C::kBK, n0);
-          tma_load_2d(&map_wlo, &full[st], sbase + 2 * C::kATileBytes + C::kBTileBytes, kb * C::kBK, n0);
+          constexpr uint32_t kWoff = (C::kTSA ? 1 : 2) * C::kATileBytes;  // W after x (and x_lo, unless TSA)
+          tma_load_2d(&map_whi, &full[st], sbase + kWoff, kb * C::kBK, n0);
+          tma_load_2d(&map_wlo, &full[st], sbase + kWoff + C::kBTileBytes, kb * C::kBK, n0);
 #pragma unroll
           for (int s = 0; s < S; ++s) issued[s] += (s == st);
           if (++st == S) {
@@ -305,8 +322,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a_hi = sb + st * C::kStageBytes;
           const uint32_t a_lo = a_hi + C::kATileBytes;
-          const uint32_t b_hi = a_hi + 2 * C::kATileBytes;
+          const uint32_t b_hi = a_hi + (C::kTSA ? 1 : 2) * C::kATileBytes;
           const uint32_t b_lo = b_hi + C::kBTileBytes;
+          if constexpr (C::kTSA) {  // A_hi / A_lo in this stage's TMEM slot
+            const uint32_t aslot = tmem_base + C::kAOffCol + st * C::kASlotCols;
+#pragma unroll
+            for (int k = 0; k < C::kBK / 8; ++k) {
+              const uint32_t koff = k * 32;
+              const uint32_t first = (kb == 0 && k == 0) ? 0u : 1u;
+              mma_tf32_ts_w(d_corr, aslot + C::kBK + 8 * k, desc_k<C::kLayout, C::kSbo>(b_hi + koff), idesc, first);
+              mma_tf32_ts_w(d_corr, aslot + 8 * k, desc_k<C::kLayout, C::kSbo>(b_lo + koff), idesc, 1u);
+              mma_tf32_ts_w(d_main, aslot + 8 * k, desc_k<C::kLayout, C::kSbo>(b_hi + koff), idesc,
+                            SPLIT ? first : 1u);
+            }
+          } else
 #pragma unroll
           for (int k = 0; k < C::kBK / 8; ++k) {
             const uint32_t koff = k * 32;  // 8 tf32 = 32 bytes along the swizzled row
@@ -369,6 +398,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             dy = tap / 3 - 1;
             dx = tap % 3 - 1;
           }
+          if constexpr (C::kTSA) {
+            // A into TMEM: this warp takes its lane quadrant's 32 rows (row = quad * 32 + lane), reads the row's
+            // 16 fp32 from the 64-byte-swizzled tile (chunk c of row r at ((c ^ ((r >> 1) & 3)) << 4)), splits
+            // them and stores hi and lo into the stage's TMEM slot. The slot is free: the producer reloaded this
+            // stage only after the MMAs that read it completed.
+            const int quad = warp & 3, row = quad * 32 + lane;
+            bool keep = true;
+            if (conv) {
+              const int rem = (ts.m0(tile) + row) % (args.conv_h * args.conv_w);
+              const int yy = rem / args.conv_w + dy, xx = rem % args.conv_w + dx;
+              keep = yy >= 0 && yy < args.conv_h && xx >= 0 && xx < args.conv_w;
+            }
+            const uint8_t* xrow = smem + st * C::kStageBytes + row * 64;
+            uint32_t hi[16], lo[16];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              float4 f = *reinterpret_cast<const float4*>(xrow + ((c ^ ((row >> 1) & 3)) << 4));
+              if (!keep) f = make_float4(0.f, 0.f, 0.f, 0.f);
+              const float fv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float hv = __uint_as_float(f32_to_tf32_rna(fv[e]));
+                hi[4 * c + e] = __float_as_uint(hv);
+                lo[4 * c + e] = f32_to_tf32_rna(fv[e] - hv);
+              }
+            }
+            const uint32_t ta =
+                tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + C::kAOffCol + st * C::kASlotCols;
+            tmem_store_x16(ta, hi);
+            tmem_store_x16(ta + C::kBK, lo);
+            tmem_store_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ready[st]);
+          } else {
           float4* xa = reinterpret_cast<float4*>(smem + st * C::kStageBytes);
           float4* xl = reinterpret_cast<float4*>(smem + st * C::kStageBytes + C::kATileBytes);
 #pragma unroll
@@ -394,6 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(&ready[st]);
+          }
         }
         if (++st == S) {
           st = 0;
@@ -883,17 +948,18 @@ const Variant* forced_variant() {
 //   leaves TMEM for two accumulator buffers at 256 columns, so the epilogue of one tile overlaps the MMAs of the
 //   next. Beyond that its error grows with K (1.1e-5 at K = 1536), and SPLIT keeps it at 4e-6.
 //   Tile width: the BN in {256, 192, 128} with the least estimated time, waves x BN x cost per column, where
-//   the cost per column (1, 1.12, 1.45 without SPLIT) was measured on B200 at the model's shapes: wider tiles read
-//   each x tile from shared memory for more columns. With SPLIT, 256-wide tiles hold all 512 TMEM columns (one
-//   buffer) and lose the overlap, so they cost more per column than 192-wide ones.
+//   the cost per column (1, 0.99, 1.45 without SPLIT; 1.12, 0.93, 1.45 with it) was measured on B200 at the
+//   model's shapes. 192-wide tiles take A from tensor memory (7 % faster than with A in shared memory); wider
+//   tiles read each x tile for more columns; with SPLIT, 256-wide tiles hold all 512 TMEM columns (one buffer)
+//   and lose the overlap of epilogue and MMAs.
 const Variant* choose_variant(int64_t M, int64_t N, int64_t K) {
   if (const Variant* f = forced_variant()) return f;
   const int split = K > 512 ? 1 : 0;
   const int64_t sms = ko::device_info().sm_count;
   const int64_t m_tiles = (M + BM - 1) / BM;
   const int bns[3] = {256, 192, 128};
-  const double cost_plain[3] = {1.0, 1.12, 1.45};
-  const double cost_split[3] = {1.12, 1.0, 1.45};
+  const double cost_plain[3] = {1.0, 0.99, 1.45};
+  const double cost_split[3] = {1.12, 0.93, 1.45};
   int best = 0;
   double best_t = 0;
   for (int i = 0; i < 3; ++i) {

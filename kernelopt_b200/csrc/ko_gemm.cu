@@ -72,9 +72,12 @@ struct Cfg {
   static constexpr uint32_t kStageBytes = (kTSA ? 1 : 2) * kATileBytes + 2 * kBTileBytes;
   static constexpr uint32_t kStatBytes = EPI == EPI_LN ? kLnStatRegion : 0;
   static constexpr int kStagesRaw = static_cast<int>((kSmemBudget - kStatBytes) / kStageBytes);
-  static constexpr int kStages = kTSA ? (kStagesRaw > 4 ? 4 : kStagesRaw) : (kStagesRaw > 8 ? 8 : kStagesRaw);
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  // The A slots form their own ring of 4 (k-block kit uses slot kit % 4), so TMA can run more stages ahead
+  // than there are slots.
+  static constexpr int kASlots = 4;
   static constexpr uint32_t kASlotCols = 2 * kBK;                    // A_hi | A_lo of one k-block in TMEM
-  static constexpr uint32_t kATmemCols = kTSA ? kStages * kASlotCols : 0;
+  static constexpr uint32_t kATmemCols = kTSA ? kASlots * kASlotCols : 0;
   static constexpr uint32_t kAccCols = BN * (SPLIT ? 2 : 1);  // TMEM columns of one tile's accumulator(s)
   static constexpr int kAccBufs = (2 * kAccCols + kATmemCols <= 512) ? 2 : 1;
   static constexpr uint32_t kAOffCol = kAccBufs * kAccCols;  // first TMEM column of the A slots
@@ -87,6 +90,7 @@ struct Cfg {
   static constexpr uint32_t kLayout = BKB == 128 ? 2u : 4u;  // descriptor layout: 128B / 64B swizzle
   static_assert(kStages >= 2, "stage does not fit");
   static_assert(kTmemNeed <= 512, "TMEM overflow");
+  static_assert((3 * kStages + 9) * 8 + 8 <= 256, "barrier area");
 };
 
 struct GemmArgs {
@@ -200,7 +204,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = bars + 3 * S;   // accumulator complete  (1 commit) x NB
   uint64_t* acc_empty = acc_full + 2;  // accumulator drained   (4 arrivals) x NB
   uint64_t* mma_done = acc_empty + 2;  // teardown drain        (1 commit)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* a_empty = mma_done + 1;    // TMEM A slot free      (1 commit) x 4
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(a_empty + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // EPI_LN: row statistics (see kLnStatBytes)
   float2* pair_stats = reinterpret_cast<float2*>(store_smem + kStoreBytes + 256);
@@ -225,6 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[a], 8);
     }
     mbar_init(mma_done, 1);
+    for (int q = 0; q < 4; ++q) mbar_init(&a_empty[q], 1);
     if (EPI == EPI_LN) {
       mbar_init(&peer_bar[0], 128);  // one arrival per lane of the peer's four first-half epilogue warps
       mbar_init(&peer_bar[1], 128);
@@ -305,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int st = 0;
       uint32_t phase = 0;
       int local = 0;
+      uint32_t kit = 0;  // running k-block index: A slot kit % 4
       bool ok = true;
       const uint32_t sb = smem_addr(smem);
       for (int tile = ts.first; tile < num_tiles && ok; tile += ts.step, ++local) {
@@ -325,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_hi = a_hi + (C::kTSA ? 1 : 2) * C::kATileBytes;
           const uint32_t b_lo = b_hi + C::kBTileBytes;
           if constexpr (C::kTSA) {  // A_hi / A_lo in this stage's TMEM slot
-            const uint32_t aslot = tmem_base + C::kAOffCol + st * C::kASlotCols;
+            const uint32_t aslot = tmem_base + C::kAOffCol + (kit & 3u) * C::kASlotCols;
 #pragma unroll
             for (int k = 0; k < C::kBK / 8; ++k) {
               const uint32_t koff = k * 32;
@@ -348,6 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                      idesc, SPLIT ? first : 1u);
           }
           mma_commit_w(&empty[st]);
+          if constexpr (C::kTSA) mma_commit_w(&a_empty[kit & 3u]);
+          ++kit;
           if (++st == S) {
             st = 0;
             phase ^= 1u;
@@ -401,9 +410,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (C::kTSA) {
             // A into TMEM: this warp takes its lane quadrant's 32 rows (row = quad * 32 + lane), reads the row's
             // 16 fp32 from the 64-byte-swizzled tile (chunk c of row r at ((c ^ ((r >> 1) & 3)) << 4)), splits
-            // them and stores hi and lo into the stage's TMEM slot. The slot is free: the producer reloaded this
-            // stage only after the MMAs that read it completed.
+            // them and stores hi and lo into TMEM slot it % 4, once the MMAs of k-block it - 4 are done with it.
             const int quad = warp & 3, row = quad * 32 + lane;
+            if (!mbar_wait(&a_empty[it & 3u], ((it >> 2) & 1u) ^ 1u, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
             bool keep = true;
             if (conv) {
               const int rem = (ts.m0(tile) + row) % (args.conv_h * args.conv_w);
@@ -425,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
             const uint32_t ta =
-                tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + C::kAOffCol + st * C::kASlotCols;
+                tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + C::kAOffCol + (it & 3u) * C::kASlotCols;
             tmem_store_x16(ta, hi);
             tmem_store_x16(ta + C::kBK, lo);
             tmem_store_wait();
@@ -948,8 +961,8 @@ const Variant* forced_variant() {
 //   leaves TMEM for two accumulator buffers at 256 columns, so the epilogue of one tile overlaps the MMAs of the
 //   next. Beyond that its error grows with K (1.1e-5 at K = 1536), and SPLIT keeps it at 4e-6.
 //   Tile width: the BN in {256, 192, 128} with the least estimated time, waves x BN x cost per column, where
-//   the cost per column (1, 0.99, 1.45 without SPLIT; 1.12, 0.93, 1.45 with it) was measured on B200 at the
-//   model's shapes. 192-wide tiles take A from tensor memory (7 % faster than with A in shared memory); wider
+//   the cost per column (1, 1.04, 1.45 without SPLIT; 1.12, 0.93, 1.45 with it) was measured on B200 at the
+//   model's shapes. 192-wide tiles take A from tensor memory (7-10 % faster than with A in shared memory); wider
 //   tiles read each x tile for more columns; with SPLIT, 256-wide tiles hold all 512 TMEM columns (one buffer)
 //   and lose the overlap of epilogue and MMAs.
 const Variant* choose_variant(int64_t M, int64_t N, int64_t K) {
@@ -958,7 +971,7 @@ const Variant* choose_variant(int64_t M, int64_t N, int64_t K) {
   const int64_t sms = ko::device_info().sm_count;
   const int64_t m_tiles = (M + BM - 1) / BM;
   const int bns[3] = {256, 192, 128};
-  const double cost_plain[3] = {1.0, 0.99, 1.45};
+  const double cost_plain[3] = {1.0, 1.04, 1.45};
   const double cost_split[3] = {1.12, 0.93, 1.45};
   int best = 0;
   double best_t = 0;

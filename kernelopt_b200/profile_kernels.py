@@ -14,6 +14,7 @@ Kernels and workloads (per frame of batch B; the algorithmic traffic or flops co
   outproj_ln  the out-projection + bias, * layer scale, + residual, LayerNorm in one kernel: x [B*1604, 384],
               W [384, 384]; flops = 2*M*384*384 (outproj_unfused: the GEMM, then the residual + LN kernel)
   fc2_ln      the same for fc2: x [B*1604, 1536], W [1536, 384] (fc2_unfused likewise)
+  qkv         the fused QKV projection: x [B*1604, 384] @ W [384, 1152] + b; flops = 2*M*384*1152
 Each timed iteration is preceded, outside the events, by a write and a read-back of a 256 MB buffer (larger
 than the 126 MB L2): every launch starts with a cold L2 that holds no dirty lines of the flush (their write-back
 would otherwise be charged to the timed kernel), and a short spin kernel holds the stream while the host enqueues the
@@ -80,6 +81,13 @@ def setup(kernel: str, b: int, dev):
             pw = K.pack_weight(w)
             fn = lambda: K.residual_layernorm(h, K.linear(x, pw), bias, scale, gamma, beta, 1e-6)  # noqa: E731
         return fn, 2.0 * m * k * 384, "flop"
+    if kernel == "qkv":
+        m = b * 1604
+        a = torch.randn(m, 384, generator=g).to(dev)
+        w = (torch.randn(384, 1152, generator=g) / 384 ** 0.5).to(dev)
+        bias = (0.01 * torch.randn(1152, generator=g)).to(dev)
+        pw = K.pack_weight(w, bias)
+        return (lambda: K.linear(a, pw)), 2.0 * m * 384 * 1152, "flop"
     if kernel == "deform":
         value = torch.randn(b, 1600, 256, generator=g).to(dev)
         loc = (torch.rand(b, 300, 16, 2, 2, generator=g) * 1.1 - 0.05).to(dev)
@@ -96,7 +104,7 @@ def setup(kernel: str, b: int, dev):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True, choices=["preprocess", "resln", "gemm", "deform", "attn", "attn_win",
-                                                             "outproj_ln", "outproj_unfused", "fc2_ln", "fc2_unfused"])
+                                                             "outproj_ln", "outproj_unfused", "fc2_ln", "fc2_unfused", "qkv"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)

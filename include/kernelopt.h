@@ -115,6 +115,19 @@ int ko_residual_layernorm(const float* h, const float* o, const float* bias, con
 int ko_layernorm(const float* x, const float* gamma, const float* beta, float eps, int64_t rows, int64_t C, int act,
                  float* y, ko_stream_t stream);
 
+/* The ViT backbone's tokens, kept in window order h: float32 [B * nwin][1 + win*win][C] (a class token, then the
+ * window's pixels row by row; windows row-major over the H x W grid, nwin = (H/win) * (W/win)), written as an
+ * NHWC image into channels [col_off, col_off + C) of out: float32 [B][H][W][ldo]:
+ *   out[b][py][px][col_off + c] = LN(h[(b*nwin + w)*(1 + win*win) + 1 + (py%win)*win + (px%win)][c])
+ * with w = (py/win)*(W/win) + px/win and LN = (v - mean) / sqrt(var + eps) * gamma + beta over C (biased variance),
+ * or the value itself when normalize == 0 (gamma, beta may then be NULL). C % 4 == 0, C <= 1024, ldo and col_off
+ * multiples of 4, 16-byte aligned pointers. Replaces the window merge (fast_rfdetr/model.py:104-105), the final
+ * LayerNorm of the tapped layers (model.py:101-103) and the channel concatenation of the projector input
+ * (model.py:161) with one pass per tapped layer. */
+int ko_window_merge_ln(const float* h, const float* gamma, const float* beta, float eps, int64_t B, int64_t H,
+                       int64_t W, int64_t win, int64_t C, int normalize, float* out, int64_t ldo, int64_t col_off,
+                       ko_stream_t stream);
+
 /* cols[(b*H + y)*W + x][tap*C + c] = x[b][y + dy - 1][x + dx - 1][c] (tap = 3*dy + dx, zero outside the image):
  * the im2col of a 3x3, stride-1, padding-1 convolution on an NHWC float32 tensor, in the column order of a conv
  * weight [out][3][3][in] flattened to [out][9*in]. C % 4 == 0; x, cols 16-byte aligned. Replaces the padded

@@ -153,3 +153,113 @@ extern "C" int ko_layernorm(const float* x, const float* gamma, const float* bet
   return dispatch(x, nullptr, nullptr, nullptr, gamma, beta, eps, rows, C, nullptr, y, act,
                   reinterpret_cast<cudaStream_t>(stream));
 }
+
+// ---------------------------------------------------------------------------------------------------------
+// Window merge (+ LayerNorm) into a channel slice: the ViT backbone keeps its tokens in window order
+// [B * nwin][1 + win*win][C] (a class token, then the window's pixels row by row; windows row-major over the
+// grid). A feature map for the projector wants them as an NHWC image; the projector then concatenates four such
+// maps along channels. This kernel writes, for every pixel (b, py, px),
+//   out[((b * H + py) * W + px) * ldo + col_off + c] = LN(h[(b * nwin + w) * (1 + win*win) + 1 + iy * win + ix][c])
+// (or the row itself with normalize = 0), where w = (py / win) * (W / win) + px / win, iy = py % win,
+// ix = px % win: the reference's window merge (fast_rfdetr/model.py:104-105) fused with the final LayerNorm of
+// the tapped layers (model.py:101-103) and the channel concatenation of the projector input (model.py:161), in
+// one pass per tapped layer. One warp per pixel; the LayerNorm is the two-pass one of residual_ln_kernel.
+// ---------------------------------------------------------------------------------------------------------
+namespace {
+
+template <int V>
+__global__ void __launch_bounds__(32 * kRowsPerBlock) window_merge_kernel(
+    const float* __restrict__ h, const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
+    int64_t pixels, int H, int W, int win, int C4, int normalize, float* __restrict__ out, int64_t ldo4,
+    int64_t col4) {
+  const int lane = threadIdx.x & 31;
+  const int64_t p = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
+  if (p >= pixels) return;
+  const int64_t b = p / (static_cast<int64_t>(H) * W);
+  const int rem = static_cast<int>(p - b * H * W);
+  const int py = rem / W, px = rem - py * W;
+  const int nwx = W / win, nwin = (H / win) * nwx;
+  const int w = (py / win) * nwx + px / win;
+  const int64_t row = (b * nwin + w) * (1 + win * win) + 1 + (py % win) * win + (px % win);
+  const float4* src = reinterpret_cast<const float4*>(h) + row * C4;
+  float4* dst = reinterpret_cast<float4*>(out) + p * ldo4 + col4;
+  float4 v[V];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + i * 32;
+    v[i] = c < C4 ? __ldg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  if (!normalize) {
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+      if (lane + i * 32 < C4) dst[lane + i * 32] = v[i];
+    return;
+  }
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, s);
+  const float inv_c = 1.0f / static_cast<float>(C4 * 4);
+  const float mean = sum * inv_c;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    if (lane + i * 32 < C4) {
+      const float dx = v[i].x - mean, dy = v[i].y - mean, dz = v[i].z - mean, dw = v[i].w - mean;
+      sq += (dx * dx + dy * dy) + (dz * dz + dw * dw);
+    }
+  }
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, s);
+  const float rstd = 1.0f / sqrtf(sq * inv_c + eps);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + i * 32;
+    if (c < C4) {
+      const float4 g = __ldg(reinterpret_cast<const float4*>(gamma) + c);
+      const float4 bt = __ldg(reinterpret_cast<const float4*>(beta) + c);
+      dst[c] = make_float4((v[i].x - mean) * rstd * g.x + bt.x, (v[i].y - mean) * rstd * g.y + bt.y,
+                           (v[i].z - mean) * rstd * g.z + bt.z, (v[i].w - mean) * rstd * g.w + bt.w);
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" int ko_window_merge_ln(const float* h, const float* gamma, const float* beta, float eps, int64_t B,
+                                  int64_t H, int64_t W, int64_t win, int64_t C, int normalize, float* out,
+                                  int64_t ldo, int64_t col_off, ko_stream_t stream) {
+  const char* who = "ko_window_merge_ln";
+  if (B < 0 || H < 1 || W < 1 || win < 1 || H % win != 0 || W % win != 0 || C < 4 || C % 4 != 0 || C > 1024 ||
+      ldo % 4 != 0 || col_off % 4 != 0 || col_off < 0 || col_off + C > ldo)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": need H, W multiples of win, C % 4 == 0, "
+                                                                "C <= 1024, col_off + C <= ldo (multiples of 4)");
+  if (B == 0) return KO_OK;
+  if (!h || !out || (normalize && (!gamma || !beta)))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": null pointer");
+  if (!ko::aligned16(h) || !ko::aligned16(out) || (normalize && (!ko::aligned16(gamma) || !ko::aligned16(beta))))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": pointers must be 16-byte aligned");
+  const int64_t pixels = B * H * W;
+  const int64_t blocks = (pixels + kRowsPerBlock - 1) / kRowsPerBlock;
+  if (blocks > 0x7fffffff) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": too many pixels");
+  const int C4 = static_cast<int>(C / 4);
+  const int V = (C4 + 31) / 32;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned g = static_cast<unsigned>(blocks);
+#define KO_WM(VV)                                                                                           \
+  window_merge_kernel<VV><<<g, 32 * kRowsPerBlock, 0, s>>>(h, gamma, beta, eps, pixels, static_cast<int>(H), \
+                                                            static_cast<int>(W), static_cast<int>(win), C4,   \
+                                                            normalize, out, ldo / 4, col_off / 4)
+  switch (V) {
+    case 1: KO_WM(1); break;
+    case 2: KO_WM(2); break;
+    case 3: KO_WM(3); break;
+    case 4: KO_WM(4); break;
+    case 5: KO_WM(5); break;
+    case 6: KO_WM(6); break;
+    case 7: KO_WM(7); break;
+    default: KO_WM(8); break;
+  }
+#undef KO_WM
+  return ko::check_launch(who);
+}

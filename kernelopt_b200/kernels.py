@@ -117,6 +117,28 @@ def layernorm(x, gamma, beta, eps, act=None, out=None):
     return out
 
 
+def window_merge_layernorm(h, grid_hw, win, out, col_off, gamma=None, beta=None, eps=1e-6, normalize=True):
+    """Writes the backbone's window-ordered tokens h [B*nwin, 1 + win*win, C] (class token first) as an NHWC
+    image into channels [col_off, col_off + C) of out [B, H, W, ldo], LayerNorm'd over C when normalize is set:
+    the window merge (model.py:104-105), the tapped layers' final LayerNorm (model.py:101-103) and the projector's
+    channel concatenation (model.py:161) in one pass. Returns out."""
+    _need(h, "h")
+    _need(out, "out")
+    gh, gw = grid_hw
+    nwin = (gh // win) * (gw // win)
+    n, lw, c = h.shape
+    if lw != 1 + win * win or n % nwin != 0:
+        raise ValueError(f"h must be [B * {nwin}, {1 + win * win}, C]")
+    b = n // nwin
+    if out.dim() != 4 or tuple(out.shape[:3]) != (b, gh, gw):
+        raise ValueError(f"out must be [{b}, {gh}, {gw}, channels]")
+    if normalize and (gamma is None or beta is None):
+        raise ValueError("gamma and beta are required to normalize")
+    call("ko_window_merge_ln", h.data_ptr(), _ptr(gamma), _ptr(beta), float(eps), b, gh, gw, win, c,
+         1 if normalize else 0, out.data_ptr(), out.shape[-1], col_off, _stream())
+    return out
+
+
 def im2col3x3(x, out=None):
     """x: float32 NHWC [B, H, W, C] -> [B*H*W, 9*C], the im2col of a 3x3 / stride 1 / padding 1 convolution in the
     column order of a [out][3][3][in] weight (the projector's mx.conv2d, model.py:154-156, as a GEMM operand)."""

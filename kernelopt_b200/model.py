@@ -186,19 +186,25 @@ class RFDETR:
         return K.layernorm(x.contiguous(), w, b, eps, act)
 
     def backbone(self, patches: torch.Tensor):
-        """patches [B, 1600, 768] -> four feature maps [B, 40, 40, C] (model.py:84-105, fused path)."""
+        """patches [B, 1600, 768] -> the four tapped feature maps [B, 40, 40, C], concatenated along channels as
+        the projector takes them: [B, 40, 40, 4C] (model.py:84-105, fused path, and the concatenation of :161).
+        Each tap is written straight into its channel slice by the window-merge (+ LayerNorm) kernel."""
         b = patches.shape[0]
         t = self.patch(patches.reshape(b * GRID * GRID, 768)).reshape(b, GRID * GRID, C) + self.pos
         t = t.reshape(b, 2, WIN, 2, WIN, C).permute(0, 1, 3, 2, 4, 5).reshape(b * 4, WIN * WIN, C)
         h = torch.cat([self.cls.expand(b * 4, 1, C), t], 1).contiguous()                      # [4B, 401, C]
         y = self._ln_op(h, self.norm1_0)
-        feats = []
+        feats = h.new_empty((b, GRID, GRID, len(TAPS) * C))
+        w, bt, eps = self.final_ln
         for i, lyr in enumerate(self.layers):
             h, y = self._vit_layer(i, lyr, h, y, b)
             if i in TAPS:
-                feats.append(y if i == 11 else self._ln_op(h, self.final_ln))
-        return [f[:, 1:].reshape(b, 2, 2, WIN, WIN, C).permute(0, 1, 3, 2, 4, 5).reshape(b, GRID, GRID, C)
-                for f in feats]
+                k = TAPS.index(i)
+                if i == 11:  # the last layer's epilogue already applied the final LayerNorm (its next norm)
+                    K.window_merge_layernorm(y, (GRID, GRID), WIN, feats, k * C, normalize=False)
+                else:
+                    K.window_merge_layernorm(h, (GRID, GRID), WIN, feats, k * C, w, bt, eps)
+        return feats
 
     def _vit_layer(self, i, lyr, h, y, b):
         """model.py:113-132: attention, residual+LN, fc1+GELU, fc2, residual+LN (next layer's norm1)."""
@@ -227,7 +233,8 @@ class RFDETR:
         return y.reshape(b, hh, ww, -1)
 
     def projector(self, feats):
-        y = self._convx(torch.cat(feats, -1), self.cv1)
+        """feats: the backbone's concatenated feature maps [B, 40, 40, 4C] -> [B, 40, 40, 256] (model.py:148-167)."""
+        y = self._convx(feats, self.cv1)
         parts = [y[..., :128], y[..., 128:]]
         for cv_a, cv_b in self.bottlenecks:
             parts.append(self._convx(self._convx(parts[-1].contiguous(), cv_a), cv_b))

@@ -185,6 +185,43 @@ def test_layernorm_plain_and_silu(cuda, c, act):
     assert_close(K.layernorm(t(x), t(g), t(b), 1e-5, act), ref, what=f"layernorm c={c} act={act}")
 
 
+@pytest.mark.parametrize("b,grid,win,c", [(2, (40, 40), 20, 384), (3, (8, 12), 4, 64), (1, (6, 6), 3, 1024),
+                                          (2, (5, 10), 5, 132)])
+def test_window_merge_layernorm(cuda, b, grid, win, c):
+    """ko_window_merge_ln: window-ordered tokens (class token first) -> NHWC channel slice of a wider buffer,
+    LayerNorm'd (1e-5 of the float64 LayerNorm) or copied (bit-exact); the channels around the slice untouched."""
+    gh, gw = grid
+    nwin = (gh // win) * (gw // win)
+    r = np.random.default_rng(c + win)
+    h = (2 * r.standard_normal((b * nwin, 1 + win * win, c)) + 0.3).astype(np.float32)
+    g = (1 + 0.1 * r.standard_normal(c)).astype(np.float32)
+    bt = (0.1 * r.standard_normal(c)).astype(np.float32)
+    _, ln = OK.residual_layernorm(h.reshape(-1, c), np.zeros((h.shape[0] * h.shape[1], c), np.float32), None, None,
+                                  g, bt, 1e-6)
+    merge = lambda a: a.reshape(b, gh // win, gw // win, 1 + win * win, c)[:, :, :, 1:].reshape(  # noqa: E731
+        b, gh // win, gw // win, win, win, c).transpose(0, 1, 3, 2, 4, 5).reshape(b, gh, gw, c)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    out = torch.full((b, gh, gw, 3 * c + 8), 7.0, device=cuda)
+    K.window_merge_layernorm(t(h), grid, win, out, 4, t(g), t(bt), 1e-6)
+    K.window_merge_layernorm(t(h), grid, win, out, 4 + 2 * c, normalize=False)
+    torch.cuda.synchronize()
+    assert_close(out[..., 4:4 + c], merge(ln.reshape(h.shape)), what="window merge + LayerNorm")
+    assert torch.equal(out[..., 4 + 2 * c:4 + 3 * c].cpu(), torch.from_numpy(merge(h)))
+    assert bool((out[..., :4] == 7).all()) and bool((out[..., 4 + c:4 + 2 * c] == 7).all())
+    assert bool((out[..., 4 + 3 * c:] == 7).all())
+
+
+def test_window_merge_rejects_bad_shapes(cuda):
+    h = torch.zeros(4, 17, 64, device=cuda)
+    out = torch.zeros(1, 8, 8, 64, device=cuda)
+    with pytest.raises(ValueError):  # the slice runs past the buffer's channels
+        K.window_merge_layernorm(h, (8, 8), 4, out, 4, normalize=False)
+    with pytest.raises(ValueError):  # tokens per window do not match win
+        K.window_merge_layernorm(h, (8, 8), 3, out, 0, normalize=False)
+    with pytest.raises(ValueError):  # normalize without gamma/beta
+        K.window_merge_layernorm(h, (8, 8), 4, out, 0)
+
+
 @pytest.mark.parametrize("shape", [(2, 7, 9, 12), (4, 40, 40, 128)])
 def test_im2col3x3_matches_padded_shifts(cuda, shape):
     """ko_im2col3x3 is a pure copy: bit-exact against the padded nine-view concatenation."""

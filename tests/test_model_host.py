@@ -74,6 +74,17 @@ def _conv3x3_ln(x, pw, gamma, beta, eps, act=None, out=None):
     return _lrln(_im2col3x3(x), pw, gamma, beta, eps, act=act, write_h=False)[1]
 
 
+def _window_merge(h, grid_hw, win, out, col_off, gamma=None, beta=None, eps=1e-6, normalize=True):
+    gh, gw = grid_hw
+    nwin = (gh // win) * (gw // win)
+    b = h.shape[0] // nwin
+    c = h.shape[-1]
+    v = F.layer_norm(h, (c,), gamma, beta, eps) if normalize else h
+    img = v[:, 1:].reshape(b, gh // win, gw // win, win, win, c).permute(0, 1, 3, 2, 4, 5).reshape(b, gh, gw, c)
+    out[..., col_off:col_off + c] = img
+    return out
+
+
 def _im2col3x3(x, out=None):
     b, h, w, c = x.shape
     xp = F.pad(x, (0, 0, 1, 1, 1, 1))
@@ -94,6 +105,7 @@ def cpu_model(monkeypatch):
     monkeypatch.setattr(K, "linear_residual_layernorm", _lrln)
     monkeypatch.setattr(K, "select_queries", _select)
     monkeypatch.setattr(K, "conv3x3_layernorm", _conv3x3_ln)
+    monkeypatch.setattr(K, "window_merge_layernorm", _window_merge)
     monkeypatch.setattr(K, "status_word", lambda *a: None)
     w = random_weights(0)
 

@@ -158,9 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
   uint64_t* q_ready = bars + 0;   // q tile written          (8 loader warps)
   uint64_t* k_full = bars + 1;    // k tile written          (4 k-loader warps)
-  uint64_t* k_empty = bars + 2;   // S MMAs done with it     (1 commit)
   uint64_t* v_full = bars + 3;    // v tile written          (4 v-loader warps)
-  uint64_t* v_empty = bars + 4;   // P.V MMAs done with it   (1 commit)
   uint64_t* s_full = bars + 5;    // S_j complete, x2        (1 commit)
   uint64_t* p_full = bars + 7;    // P_j written             (4 softmax warps)
   uint64_t* o_full = bars + 8;    // O_j complete, x2        (1 commit)
@@ -179,9 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
   if (threadIdx.x == 0) {
     mbar_init(q_ready, 8);
     mbar_init(k_full, 4);
-    mbar_init(k_empty, 1);
     mbar_init(v_full, 4);
-    mbar_init(v_empty, 1);
     mbar_init(p_full, 4);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -240,8 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
           mma_tf32_w(d, dq_hi + off, dk_lo + off, idesc_s, 1u);
           mma_tf32_w(d, dq_hi + off, dk_hi + off, idesc_s, 1u);
         }
-        mma_commit_w(&s_full[j & 1]);
-        mma_commit_w(k_empty);
+        mma_commit_w(&s_full[j & 1]);  // the k loaders wait on it too (S_j done = k tile j free)
       };
       bool ok = warp_wait(q_ready, 0, abort_flag) && warp_wait(k_full, 0, abort_flag);
       if (ok) {
@@ -265,22 +260,38 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
         const uint32_t p_hi = tmem + kColS + static_cast<uint32_t>(j & 1) * BKEY;
         const int ksteps = (keys_of(j) + 7) >> 3;
         // The P_lo products first, then a commit that hands the P_lo columns back to the softmax warps: they
-        // write P_{j+1} while the P_hi products of this block (two thirds of its MMAs) still run.
+        // write P_{j+1} while the P_hi products of this block (two thirds of its MMAs) still run. A full block's
+        // MMAs are issued from fully unrolled code: a 128 x HD x 8 product takes the tensor pipe only 32 cycles
+        // (HD 64), and a rolled loop's per-MMA address arithmetic would make the issue, not the pipe, the limit.
+        if (ksteps == BKEY / 8) {
+#pragma unroll
+          for (int kk = 0; kk < BKEY / 8; ++kk) {  // 8 keys per k-step
+            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
+            mma_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
+          }
+          mma_commit_w(plo_free);
+#pragma unroll
+          for (int kk = 0; kk < BKEY / 8; ++kk) {
+            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
+            mma_tf32_ts_w(d, p_hi + 8 * kk, dv_lo + off, idesc_o, 1u);
+            mma_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + off, idesc_o, 1u);
+          }
+        } else {  // a short last block
 #pragma unroll 1
-        for (int kk = 0; kk < ksteps; ++kk) {  // 8 keys per k-step
-          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
-          mma_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
-        }
-        mma_commit_w(plo_free);
+          for (int kk = 0; kk < ksteps; ++kk) {
+            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
+            mma_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
+          }
+          mma_commit_w(plo_free);
 #pragma unroll 1
-        for (int kk = 0; kk < ksteps; ++kk) {
-          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
-          const uint32_t phi = p_hi + 8 * kk;
-          mma_tf32_ts_w(d, phi, dv_lo + off, idesc_o, 1u);
-          mma_tf32_ts_w(d, phi, dv_hi + off, idesc_o, 1u);
+          for (int kk = 0; kk < ksteps; ++kk) {
+            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
+            mma_tf32_ts_w(d, p_hi + 8 * kk, dv_lo + off, idesc_o, 1u);
+            mma_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + off, idesc_o, 1u);
+          }
         }
+        // One commit per event: the v loaders wait on o_full as well (P_j.V_j done = v tile j free).
         mma_commit_w(&o_full[j & 1]);
-        mma_commit_w(v_empty);
       }
       // Drain: every MMA this warp issued completes before tensor memory is released.
       mma_commit_w(mma_done);
@@ -467,7 +478,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
         if (lane == 0) mbar_arrive(k_full);
       }
       for (int j = 1; j < nkb && kok; ++j) {
-        if (!mbar_wait(k_empty, (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag)) break;
+        // k tile j overwrites tile j-1: S_{j-1} must be complete
+        if (!mbar_wait(&s_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag)) break;
 #pragma unroll
         for (int i = 0; i < kTileChunks; ++i) {
           const int idx = i * kGroup + g, r = idx / Q4, c = idx % Q4;
@@ -500,7 +512,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
       load(0);
       const bool vok = write_q();
       for (int j = 0; j < nkb && vok; ++j) {
-        if (!mbar_wait(v_empty, (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag)) break;
+        // v tile j overwrites tile j-1: P_{j-1}.V_{j-1} must be complete
+        if (j >= 1 && !mbar_wait(&o_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag)) break;
 #pragma unroll
         for (int i = 0; i < kTileChunks; ++i) {
           const int idx = i * kGroup + g, key = idx & (BKEY - 1), dq = idx / BKEY;

@@ -7,8 +7,10 @@
 // ViT backbone (fast_rfdetr/model.py:107-110 and 119-120, windowed and global layers) and in the decoder's self-attention
 // (self_attn, model.py:232-239, 8 heads of 32), computed in fp32 there. No mask, no dropout.
 //
-// Precision: every operand is split v = hi + lo (hi = tf32_rn(v), lo = tf32_rn(v - hi)) and the tensor cores
-// accumulate hi*hi + hi*lo + lo*hi in fp32 (Ootomo & Yokota's error-compensated 3xTF32). The softmax runs in
+// Precision: every operand is split v = hi + lo and the tensor cores accumulate hi*hi + hi*lo + lo*hi in fp32
+// (Ootomo & Yokota's error-compensated 3xTF32). q and k, whose products the exponential amplifies, use
+// hi = tf32_rn(v); p and v use hi = v itself, which the tensor core reads truncated to tf32, and lo = the exact
+// remainder below that truncation (two operations per element instead of three; error below 2^-20 per term). The softmax runs in
 // fp32 registers with the running maximum / running sum of the online (flash) formulation; each key block's
 // P.V product lands in a fresh tensor-memory accumulator and is added into the fp32 output row in registers,
 // so the long sum over keys is a plain fp32 register sum, not a tensor-core accumulation.
@@ -139,6 +141,18 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const bool ok = mbar_wait(bar, parity, abort);
   return __all_sync(0xffffffffu, ok);
+}
+
+// The part of v below its tf32 truncation: v - (v with the low 13 mantissa bits cleared), exact in fp32. P is kept
+// as v in the P_hi slot (the tensor core reads a tf32 operand from the top 19 bits of the word, i.e. truncates)
+// and this tail in P_lo, so P = P_hi + P_lo exactly before the MMA truncates P_lo (an error below 2^-20 P).
+__device__ __forceinline__ float tf32_tail(float v) { return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
+
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 // 2^x by the MUFU (ex2.approx, relative error below 2^-22 over the range used here: x <= 0).
@@ -359,14 +373,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
           for (int e = 0; e < 16; ++e)
             if (e >= nv) r[e] = __float_as_uint(-INFINITY);
         }
-        float c0 = fmaxf(__uint_as_float(r[0]), __uint_as_float(r[1]));
-        float c1 = fmaxf(__uint_as_float(r[2]), __uint_as_float(r[3]));
-#pragma unroll
-        for (int e = 4; e < 16; e += 4) {
-          c0 = fmaxf(c0, fmaxf(__uint_as_float(r[e]), __uint_as_float(r[e + 1])));
-          c1 = fmaxf(c1, fmaxf(__uint_as_float(r[e + 2]), __uint_as_float(r[e + 3])));
-        }
-        const float cmax = fmaxf(c0, c1) * a.scale_log2;
+        const float* f = reinterpret_cast<const float*>(r);
+        const float m0 = fmax3(f[0], f[1], f[2]), m1 = fmax3(f[3], f[4], f[5]), m2 = fmax3(f[6], f[7], f[8]);
+        const float m3 = fmax3(f[9], f[10], f[11]), m4 = fmax3(f[12], f[13], f[14]);
+        const float cmax = fmaxf(fmax3(m0, m1, m2), fmax3(m3, m4, f[15])) * a.scale_log2;
         const bool raise = cmax > mb + kRaise;
         if (__any_sync(0xffffffffu, raise)) {  // rare after the first chunk: raise the offset, rescale chunks < c
           const float m_new = raise ? cmax : mb;
@@ -375,16 +385,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
 #pragma unroll 1
           for (int cc = 0; cc < c; ++cc) {
             uint32_t h2[16], l2[16];
-            tmem_ld_32x32b_x16(srow + 16 * cc, h2);
-            tmem_ld_32x32b_x16(plrow + 16 * cc, l2);
+            tmem_ld_32x32b_x16(srow + 16 * cc, h2);  // the P_hi slot holds P itself
             tmem_ld_wait_regs16(h2);
-            tmem_ld_wait_regs16(l2);
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              float phi, plo;
-              split_tf32((__uint_as_float(h2[e]) + __uint_as_float(l2[e])) * beta, phi, plo);
-              h2[e] = __float_as_uint(phi);
-              l2[e] = __float_as_uint(plo);
+              const float p = __uint_as_float(h2[e]) * beta;
+              h2[e] = __float_as_uint(p);
+              l2[e] = __float_as_uint(tf32_tail(p));
             }
             tmem_st_32x32b_x16(srow + 16 * cc, h2);
             tmem_st_32x32b_x16(plrow + 16 * cc, l2);
@@ -396,10 +403,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
         for (int e = 0; e < 16; ++e) {
           const float p = fast_exp2(fmaf(__uint_as_float(r[e]), a.scale_log2, -mb));  // 0 for masked keys
           ls += p;
-          float phi, plo;
-          split_tf32(p, phi, plo);
-          r[e] = __float_as_uint(phi);
-          lo[e] = __float_as_uint(plo);
+          r[e] = __float_as_uint(p);  // read by the MMA as its top 19 bits: P_hi = P truncated to tf32
+          lo[e] = __float_as_uint(tf32_tail(p));
         }
         tmem_st_32x32b_x16(srow + 16 * c, r);
         tmem_st_32x32b_x16(plrow + 16 * c, lo);
@@ -523,8 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
           for (int e = 0; e < 4; ++e) {
             const int d = 4 * dq + e;
             const uint32_t off = base + sw128(d, (key & 31) >> 2);
-            float hi, lo;
-            split_tf32(src[e], hi, lo);
+            const float hi = src[e], lo = tf32_tail(src[e]);  // v itself as hi: P.V errors are not amplified
             *reinterpret_cast<float*>(smem + C::kOffVhi + off) = hi;
             *reinterpret_cast<float*>(smem + C::kOffVlo + off) = lo;
           }

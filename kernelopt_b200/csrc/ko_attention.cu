@@ -314,13 +314,11 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
     }
   } else if (warp < kLoadWarp0) {
     // ---------------- softmax + output, one thread per query row ----------------
-    // Block j, one pass over S_j: once P_{j-1}.V_{j-1}'s P_lo products are done (the P_lo columns are free), each
-    // 16-key chunk becomes P = exp2(S * c - m) as tf32 hi / lo in tensor memory. The exponent offset m is raised
-    // lazily: only when a chunk's maximum exceeds it by more than kRaise (so P <= 2^kRaise), and then the chunks
-    // of this block already written are rescaled in place. The final o / l is the same for any offset, since
-    // numerator and denominator share it. Then, once all of P_{j-1}.V_{j-1} is complete, o = o * alpha + that
-    // block's product.
-    constexpr float kRaise = 8.0f;
+    // Block j, two passes over S_j in tensor memory (a 16-column load costs about 9 cycles): the first finds the
+    // row maximum, which sets the block's offset m = max(m, block maximum) (online softmax, P <= 1); once
+    // P_{j-1}.V_{j-1}'s P_lo products are done (the P_lo columns are free) the second turns each 16-key chunk
+    // into P = exp2(S * c - m), written as P itself and its tf32 tail. The max pass overlaps that wait. Then, once
+    // all of P_{j-1}.V_{j-1} is complete, o = o * alpha + that block's product.
     const int quad = warp & 3;  // tensor-memory lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
@@ -351,20 +349,16 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
         ok = false;
         break;
       }
-      if (j >= 1 && !warp_wait(plo_free, static_cast<uint32_t>(j - 1) & 1u, abort_flag)) {
-        ok = false;
-        break;
-      }
       tc_fence_after();
       const uint32_t srow = trow + kColS + static_cast<uint32_t>(j & 1) * BKEY;
       const uint32_t plrow = trow + kColPlo;
       const int valid = min(BKEY, a.L - j * BKEY);
       const int chunks = (valid + 15) >> 4;  // 16-column chunks that hold keys of this block
-      float mb = m;                          // offset of this block's P
-      float ls = 0.f;
+      // pass 1: the block's row maximum
+      float mx = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < chunks; ++c) {
-        uint32_t r[16], lo[16];
+        uint32_t r[16];
         tmem_ld_32x32b_x16(srow + 16 * c, r);
         tmem_ld_wait_regs16(r);
         const int nv = valid - 16 * c;  // keys of this chunk (>= 16 except in a short last block)
@@ -376,39 +370,34 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
         const float* f = reinterpret_cast<const float*>(r);
         const float m0 = fmax3(f[0], f[1], f[2]), m1 = fmax3(f[3], f[4], f[5]), m2 = fmax3(f[6], f[7], f[8]);
         const float m3 = fmax3(f[9], f[10], f[11]), m4 = fmax3(f[12], f[13], f[14]);
-        const float cmax = fmaxf(fmax3(m0, m1, m2), fmax3(m3, m4, f[15])) * a.scale_log2;
-        const bool raise = cmax > mb + kRaise;
-        if (__any_sync(0xffffffffu, raise)) {  // rare after the first chunk: raise the offset, rescale chunks < c
-          const float m_new = raise ? cmax : mb;
-          const float beta = fast_exp2(mb - m_new);  // 0 when mb was -inf (nothing written yet)
-          tmem_st_wait();
+        mx = fmax3(mx, fmax3(m0, m1, m2), fmax3(m3, m4, f[15]));
+      }
+      const float mb = fmaxf(m, mx * a.scale_log2);  // offset of this block's P
+      if (j >= 1 && !warp_wait(plo_free, static_cast<uint32_t>(j - 1) & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // pass 2: P and its tail; two partial sums shorten the dependent chain of additions
+      float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll 1
-          for (int cc = 0; cc < c; ++cc) {
-            uint32_t h2[16], l2[16];
-            tmem_ld_32x32b_x16(srow + 16 * cc, h2);  // the P_hi slot holds P itself
-            tmem_ld_wait_regs16(h2);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const float p = __uint_as_float(h2[e]) * beta;
-              h2[e] = __float_as_uint(p);
-              l2[e] = __float_as_uint(tf32_tail(p));
-            }
-            tmem_st_32x32b_x16(srow + 16 * cc, h2);
-            tmem_st_32x32b_x16(plrow + 16 * cc, l2);
-          }
-          ls *= beta;
-          mb = m_new;
-        }
+      for (int c = 0; c < chunks; ++c) {
+        uint32_t r[16], lo[16];
+        tmem_ld_32x32b_x16(srow + 16 * c, r);
+        tmem_ld_wait_regs16(r);
+        const int nv = valid - 16 * c;
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p = fast_exp2(fmaf(__uint_as_float(r[e]), a.scale_log2, -mb));  // 0 for masked keys
-          ls += p;
+          float p = fast_exp2(fmaf(__uint_as_float(r[e]), a.scale_log2, -mb));
+          if (e >= nv) p = 0.f;  // keys past the end of a short last block
+          if (e & 1) ls1 += p; else ls0 += p;
           r[e] = __float_as_uint(p);  // read by the MMA as its top 19 bits: P_hi = P truncated to tf32
           lo[e] = __float_as_uint(tf32_tail(p));
         }
         tmem_st_32x32b_x16(srow + 16 * c, r);
         tmem_st_32x32b_x16(plrow + 16 * c, lo);
       }
+      const float ls = ls0 + ls1;
       tmem_st_wait();
       const float alpha = fast_exp2(m - mb);  // 0 for the first block (m = -inf)
       l = l * alpha + ls;

@@ -22,9 +22,11 @@
 //   warps 1-4   softmax + output: one thread per query row. Reads S from tensor memory, updates the row's running
 //               max / sum, writes P (hi and lo) back into tensor memory for the P.V MMA, then adds O_j into the
 //               output row it keeps in registers. At the end divides by the sum and stores the row.
-//   warps 5-12  loaders: q, k and v rows straight from global memory (128-bit loads; warps 5-8 stream k, 9-12
-//               stream v, each holding the next key block in registers while the current one is in use), split
-//               into hi / lo and written into shared memory in the MMA's 128-byte-swizzled K-major layout. v is
+//   warps 5-12  loaders: the q tile and the first k tile arrive by TMA and are split in place, q by warps 9-12 and
+//               k by warps 5-8 at the same time; the other key blocks stream from global memory (128-bit loads;
+//               warps 5-8 stream k, 9-12 stream v, each holding the next key block in registers while the current
+//               one is in use), split into hi / lo and written into shared memory in the MMA's 128-byte-swizzled
+//               K-major layout. v is
 //               written transposed (head dim x keys), the K-major form of the P.V product's B operand.
 // Tensor memory (512 columns): two S / P_hi buffers [0,256), P_lo [256,384), two O_j buffers of HD columns from
 // 384. With two S buffers the tensor cores compute S_{j+1} while the softmax warps work on block j, and P_j.V_j
@@ -170,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
-  uint64_t* q_ready = bars + 0;   // q tile written          (8 loader warps)
+  uint64_t* q_ready = bars + 0;   // q tile split            (4 v-loader warps)
   uint64_t* k_full = bars + 1;    // k tile written          (4 k-loader warps)
   uint64_t* v_full = bars + 3;    // v tile written          (4 v-loader warps)
   uint64_t* s_full = bars + 5;    // S_j complete, x2        (1 commit)
@@ -189,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
   const int nkb = a.n_kblocks;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_ready, 8);
+    mbar_init(q_ready, 4);
     mbar_init(k_full, 4);
     mbar_init(v_full, 4);
     mbar_init(p_full, 4);
@@ -423,9 +425,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
     }
   } else {
     // ---------------- loaders ----------------
-    // All 8 warps split the q tile (brought in by TMA) in place; warps 5-8 stream the k tiles and warps 9-12 the
-    // v tiles, each group holding its next tile in registers while the current one is in use. The first k tile
-    // also comes by TMA and is split in place by the k group.
+    // The q tile and the first k tile come by TMA; the v group (warps 9-12) splits q in place while the k group
+    // (warps 5-8) splits the first k tile, so S_0 waits for one split, not two in a row. Then warps 5-8 stream the
+    // k tiles and warps 9-12 the v tiles, each group holding its next tile in registers while the current one is
+    // in use.
     const int t = threadIdx.x - kLoadWarp0 * 32;  // 0..255
     constexpr int Q4 = HD / 4;                   // float4 per row
     // hi in place, lo at the same offset in the lo buffer (the split is elementwise: any cover of the tile works)
@@ -444,15 +447,15 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
       fence_proxy_async_smem();
       __syncwarp();
     };
-    auto write_q = [&]() -> bool {
-      if (!mbar_wait(q_tma, 0, abort_flag)) return false;
-      split_in_place(0, C::kOffQlo, static_cast<int>(C::kQBytes / 16), t, kLoadThreads);
-      if (lane == 0) mbar_arrive(q_ready);
-      return true;
-    };
     constexpr int kGroup = kLoadThreads / 2;       // 128 threads per group
     constexpr int kTileChunks = BKEY * HD / 4 / kGroup;
     const int g = t & (kGroup - 1);
+    auto write_q = [&]() -> bool {
+      if (!mbar_wait(q_tma, 0, abort_flag)) return false;
+      split_in_place(0, C::kOffQlo, static_cast<int>(C::kQBytes / 16), g, kGroup);
+      if (lane == 0) mbar_arrive(q_ready);
+      return true;
+    };
     float4 reg[kTileChunks];
     if (t < kGroup) {
       // k tiles: row-major chunks (a warp reads whole rows), stored K-major with the 128-byte swizzle
@@ -465,12 +468,14 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
                             : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       };
-      if (nkb > 1) load(1);
-      bool kok = write_q() && mbar_wait(k0_tma, 0, abort_flag);
+      // The first k tile is split as soon as it lands (the v group splits q meanwhile); the prefetch of the
+      // next tile into registers follows, so that its loads do not compete with the split.
+      bool kok = mbar_wait(k0_tma, 0, abort_flag);
       if (kok) {
         split_in_place(C::kOffKhi, C::kOffKlo, static_cast<int>(C::kKBytes / 16), g, kGroup);
         if (lane == 0) mbar_arrive(k_full);
       }
+      if (nkb > 1) load(1);
       for (int j = 1; j < nkb && kok; ++j) {
         // k tile j overwrites tile j-1: S_{j-1} must be complete
         if (!mbar_wait(&s_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag)) break;
@@ -503,8 +508,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
                             : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       };
-      load(0);
       const bool vok = write_q();
+      load(0);
       for (int j = 0; j < nkb && vok; ++j) {
         // v tile j overwrites tile j-1: P_{j-1}.V_{j-1} must be complete
         if (j >= 1 && !mbar_wait(&o_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag)) break;

@@ -128,6 +128,16 @@ int ko_window_merge_ln(const float* h, const float* gamma, const float* beta, fl
                        int64_t W, int64_t win, int64_t C, int normalize, float* out, int64_t ldo, int64_t col_off,
                        ko_stream_t stream);
 
+/* The backbone's entry: t: float32 [B][H][W][C] (the patch embedding, bias included), pos: [H][W][C], cls: [C]
+ * -> h: float32 [B * nwin][1 + win*win][C] in window order (nwin = (H/win) * (W/win), windows row-major, each
+ * row block led by the class token), h = cls for the first row of a window and t + pos for its pixels (row by
+ * row), and y = LayerNorm(h) over C with gamma, beta, eps (biased variance). C % 4 == 0, C <= 1024, 16-byte
+ * aligned pointers. Replaces the pos add, window partition and class-token concatenation of fast_rfdetr/model.py:88-90
+ * and the first layer's LayerNorm (model.py:94) with one pass. */
+int ko_window_partition_ln(const float* t, const float* pos, const float* cls, const float* gamma,
+                           const float* beta, float eps, int64_t B, int64_t H, int64_t W, int64_t win, int64_t C,
+                           float* h, float* y, ko_stream_t stream);
+
 /* cols[(b*H + y)*W + x][tap*C + c] = x[b][y + dy - 1][x + dx - 1][c] (tap = 3*dy + dx, zero outside the image):
  * the im2col of a 3x3, stride-1, padding-1 convolution on an NHWC float32 tensor, in the column order of a conv
  * weight [out][3][3][in] flattened to [out][9*in]. C % 4 == 0; x, cols 16-byte aligned. Replaces the padded

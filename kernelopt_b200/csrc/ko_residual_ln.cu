@@ -263,3 +263,120 @@ extern "C" int ko_window_merge_ln(const float* h, const float* gamma, const floa
 #undef KO_WM
   return ko::check_launch(who);
 }
+
+// ---------------------------------------------------------------------------------------------------------
+// Window partition of the patch embedding + the first layer's LayerNorm (ko_window_partition_ln).
+// Semantics: fast_rfdetr/model.py:88-90 and :94 — t + pos over the H x W token grid, cut into (H/win) x (W/win)
+// windows of win x win tokens (row-major), each window preceded by the class token, then y = LayerNorm(h) with
+// the first layer's norm1. One warp per output token row: it reads the patch-embedding row and the pos row (or the
+// class token), writes h and the two-pass LayerNorm of it. Replaces the pos add, the window permute copy, the class
+// token concatenation and the separate LayerNorm pass.
+// ---------------------------------------------------------------------------------------------------------
+namespace {
+
+template <int V>
+__global__ void __launch_bounds__(32 * kRowsPerBlock) window_partition_kernel(
+    const float* __restrict__ t, const float* __restrict__ pos, const float* __restrict__ cls,
+    const float* __restrict__ gamma, const float* __restrict__ beta, float eps, int64_t rows, int H, int W, int win,
+    int C4, float* __restrict__ h, float* __restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int per = 1 + win * win, nwx = W / win, nwin = (H / win) * nwx;
+  const int64_t n = row / per;  // window index over the batch
+  const int r = static_cast<int>(row - n * per);
+  const float4* src;
+  const float4* add = nullptr;
+  if (r == 0) {
+    src = reinterpret_cast<const float4*>(cls);
+  } else {
+    const int64_t bi = n / nwin;
+    const int w = static_cast<int>(n - bi * nwin);
+    const int py = (w / nwx) * win + (r - 1) / win, px = (w % nwx) * win + (r - 1) % win;
+    src = reinterpret_cast<const float4*>(t) + ((bi * H + py) * W + px) * C4;
+    add = reinterpret_cast<const float4*>(pos) + (static_cast<int64_t>(py) * W + px) * C4;
+  }
+  float4 v[V];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + i * 32;
+    v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < C4) {
+      v[i] = __ldg(src + c);
+      if (add) {
+        const float4 p = __ldg(add + c);
+        v[i] = make_float4(v[i].x + p.x, v[i].y + p.y, v[i].z + p.z, v[i].w + p.w);
+      }
+      reinterpret_cast<float4*>(h)[row * C4 + c] = v[i];
+    }
+    sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, s);
+  const float inv_c = 1.0f / static_cast<float>(C4 * 4);
+  const float mean = sum * inv_c;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    if (lane + i * 32 < C4) {
+      const float dx = v[i].x - mean, dy = v[i].y - mean, dz = v[i].z - mean, dw = v[i].w - mean;
+      sq += (dx * dx + dy * dy) + (dz * dz + dw * dw);
+    }
+  }
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, s);
+  const float rstd = 1.0f / sqrtf(sq * inv_c + eps);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = lane + i * 32;
+    if (c < C4) {
+      const float4 g = __ldg(reinterpret_cast<const float4*>(gamma) + c);
+      const float4 bt = __ldg(reinterpret_cast<const float4*>(beta) + c);
+      reinterpret_cast<float4*>(y)[row * C4 + c] =
+          make_float4((v[i].x - mean) * rstd * g.x + bt.x, (v[i].y - mean) * rstd * g.y + bt.y,
+                      (v[i].z - mean) * rstd * g.z + bt.z, (v[i].w - mean) * rstd * g.w + bt.w);
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" int ko_window_partition_ln(const float* t, const float* pos, const float* cls, const float* gamma,
+                                      const float* beta, float eps, int64_t B, int64_t H, int64_t W, int64_t win,
+                                      int64_t C, float* h, float* y, ko_stream_t stream) {
+  const char* who = "ko_window_partition_ln";
+  if (B < 0 || H < 1 || W < 1 || win < 1 || H % win != 0 || W % win != 0 || C < 4 || C % 4 != 0 || C > 1024 ||
+      H * W > (int64_t(1) << 30))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT,
+                    std::string(who) + ": need H, W multiples of win, C % 4 == 0 and C <= 1024");
+  if (B == 0) return KO_OK;
+  if (!t || !pos || !cls || !gamma || !beta || !h || !y)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": null pointer");
+  if (!ko::aligned16(t) || !ko::aligned16(pos) || !ko::aligned16(cls) || !ko::aligned16(gamma) ||
+      !ko::aligned16(beta) || !ko::aligned16(h) || !ko::aligned16(y))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": pointers must be 16-byte aligned");
+  const int64_t rows = B * (H / win) * (W / win) * (1 + win * win);
+  const int64_t blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
+  if (blocks > 0x7fffffff) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": too many rows");
+  const int C4 = static_cast<int>(C / 4);
+  const int V = (C4 + 31) / 32;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned g = static_cast<unsigned>(blocks);
+#define KO_WP(VV)                                                                                                \
+  window_partition_kernel<VV><<<g, 32 * kRowsPerBlock, 0, s>>>(t, pos, cls, gamma, beta, eps, rows,                \
+                                                               static_cast<int>(H), static_cast<int>(W),          \
+                                                               static_cast<int>(win), C4, h, y)
+  switch (V) {
+    case 1: KO_WP(1); break;
+    case 2: KO_WP(2); break;
+    case 3: KO_WP(3); break;
+    case 4: KO_WP(4); break;
+    case 5: KO_WP(5); break;
+    case 6: KO_WP(6); break;
+    case 7: KO_WP(7); break;
+    default: KO_WP(8); break;
+  }
+#undef KO_WP
+  return ko::check_launch(who);
+}

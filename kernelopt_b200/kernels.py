@@ -139,6 +139,31 @@ def window_merge_layernorm(h, grid_hw, win, out, col_off, gamma=None, beta=None,
     return out
 
 
+def window_partition_layernorm(t, pos, cls, win, gamma, beta, eps=1e-6, h=None, y=None):
+    """The backbone's entry in one pass: t [B, H, W, C] (patch embedding) plus pos [H, W, C], cut into win x win
+    windows each led by the class token cls [C] -> (h [B*nwin, 1 + win*win, C], LayerNorm(h)) — the pos add,
+    window partition and concatenation of model.py:88-90 and the first LayerNorm of model.py:94."""
+    for a, n in ((t, "t"), (pos, "pos"), (cls, "cls"), (gamma, "gamma"), (beta, "beta")):
+        _need(a, n)
+    if t.dim() != 4:
+        raise ValueError("t must be [B, H, W, C]")
+    b, gh, gw, c = t.shape
+    if tuple(pos.shape) != (gh, gw, c) or cls.numel() != c:
+        raise ValueError("pos must be [H, W, C] and cls [C]")
+    if gh % win or gw % win:
+        raise ValueError("H and W must be multiples of win")
+    shape = (b * (gh // win) * (gw // win), 1 + win * win, c)
+    h = torch.empty(shape, dtype=torch.float32, device=t.device) if h is None else h
+    y = torch.empty(shape, dtype=torch.float32, device=t.device) if y is None else y
+    _need(h, "h")
+    _need(y, "y")
+    if tuple(h.shape) != shape or tuple(y.shape) != shape:
+        raise ValueError(f"h and y must be {list(shape)}")
+    call("ko_window_partition_ln", t.data_ptr(), pos.data_ptr(), cls.data_ptr(), gamma.data_ptr(),
+         beta.data_ptr(), float(eps), b, gh, gw, win, c, h.data_ptr(), y.data_ptr(), _stream())
+    return h, y
+
+
 def im2col3x3(x, out=None):
     """x: float32 NHWC [B, H, W, C] -> [B*H*W, 9*C], the im2col of a 3x3 / stride 1 / padding 1 convolution in the
     column order of a [out][3][3][in] weight (the projector's mx.conv2d, model.py:154-156, as a GEMM operand)."""

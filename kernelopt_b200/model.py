@@ -190,10 +190,10 @@ class RFDETR:
         the projector takes them: [B, 40, 40, 4C] (model.py:84-105, fused path, and the concatenation of :161).
         Each tap is written straight into its channel slice by the window-merge (+ LayerNorm) kernel."""
         b = patches.shape[0]
-        t = self.patch(patches.reshape(b * GRID * GRID, 768)).reshape(b, GRID * GRID, C) + self.pos
-        t = t.reshape(b, 2, WIN, 2, WIN, C).permute(0, 1, 3, 2, 4, 5).reshape(b * 4, WIN * WIN, C)
-        h = torch.cat([self.cls.expand(b * 4, 1, C), t], 1).contiguous()                      # [4B, 401, C]
-        y = self._ln_op(h, self.norm1_0)
+        t = self.patch(patches.reshape(b * GRID * GRID, 768)).reshape(b, GRID, GRID, C)
+        w0, b0, eps0 = self.norm1_0        # + pos, 2 x 2 windows led by the class token, first LayerNorm: one pass
+        h, y = K.window_partition_layernorm(t, self.pos.view(GRID, GRID, C), self.cls.reshape(C), WIN, w0, b0,
+                                            eps0)                                               # [4B, 401, C]
         feats = h.new_empty((b, GRID, GRID, len(TAPS) * C))
         w, bt, eps = self.final_ln
         for i, lyr in enumerate(self.layers):

@@ -211,6 +211,41 @@ def test_window_merge_layernorm(cuda, b, grid, win, c):
     assert bool((out[..., 4 + 3 * c:] == 7).all())
 
 
+@pytest.mark.parametrize("b,grid,win,c", [(2, (40, 40), 20, 384), (3, (8, 12), 4, 64), (1, (6, 6), 3, 1024),
+                                          (2, (5, 10), 5, 132)])
+def test_window_partition_layernorm(cuda, b, grid, win, c):
+    """ko_window_partition_ln: (t + pos) cut into windows led by the class token — bit-exact against the same
+    additions in float32 — and its LayerNorm within 1e-5 of float64."""
+    gh, gw = grid
+    r = np.random.default_rng(c + 3 * win)
+    t = (2 * r.standard_normal((b, gh, gw, c)) + 0.3).astype(np.float32)
+    pos = (0.5 * r.standard_normal((gh, gw, c))).astype(np.float32)
+    cls = r.standard_normal(c).astype(np.float32)
+    g = (1 + 0.1 * r.standard_normal(c)).astype(np.float32)
+    bt = (0.1 * r.standard_normal(c)).astype(np.float32)
+    v = (t + pos).reshape(b, gh // win, win, gw // win, win, c).transpose(0, 1, 3, 2, 4, 5).reshape(-1, win * win, c)
+    ref_h = np.concatenate([np.broadcast_to(cls, (v.shape[0], 1, c)), v], 1)
+    _, ref_y = OK.residual_layernorm(ref_h.reshape(-1, c), np.zeros((ref_h.size // c, c), np.float32), None, None,
+                                     g, bt, 1e-6)
+    tt = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    h, y = K.window_partition_layernorm(tt(t), tt(pos), tt(cls), win, tt(g), tt(bt), 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(h.cpu(), torch.from_numpy(np.ascontiguousarray(ref_h)))
+    assert_close(y, ref_y.reshape(ref_h.shape), what="window partition + LayerNorm")
+
+
+def test_window_partition_rejects_bad_shapes(cuda):
+    t = torch.zeros(1, 8, 8, 64, device=cuda)
+    pos, cls, g = torch.zeros(8, 8, 64, device=cuda), torch.zeros(64, device=cuda), torch.ones(64, device=cuda)
+    with pytest.raises(ValueError):  # the grid is not a multiple of win
+        K.window_partition_layernorm(t, pos, cls, 3, g, g)
+    with pytest.raises(ValueError):  # pos of the wrong grid
+        K.window_partition_layernorm(t, pos[:4], cls, 4, g, g)
+    with pytest.raises(ValueError):  # C not a multiple of 4 (checked by the entry point)
+        K.window_partition_layernorm(t[..., :62].contiguous(), pos[..., :62].contiguous(), cls[:62].contiguous(), 4,
+                                     g[:62].contiguous(), g[:62].contiguous())
+
+
 def test_window_merge_rejects_bad_shapes(cuda):
     h = torch.zeros(4, 17, 64, device=cuda)
     out = torch.zeros(1, 8, 8, 64, device=cuda)

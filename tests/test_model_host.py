@@ -85,6 +85,14 @@ def _window_merge(h, grid_hw, win, out, col_off, gamma=None, beta=None, eps=1e-6
     return out
 
 
+def _window_partition(t, pos, cls, win, gamma, beta, eps=1e-6, h=None, y=None):
+    b, gh, gw, c = t.shape
+    v = (t + pos).reshape(b, gh // win, win, gw // win, win, c).permute(0, 1, 3, 2, 4, 5)
+    v = v.reshape(-1, win * win, c)
+    hh = torch.cat([cls.reshape(1, 1, c).expand(v.shape[0], 1, c), v], 1)
+    return hh, F.layer_norm(hh, (c,), gamma, beta, eps)
+
+
 def _im2col3x3(x, out=None):
     b, h, w, c = x.shape
     xp = F.pad(x, (0, 0, 1, 1, 1, 1))
@@ -106,6 +114,7 @@ def cpu_model(monkeypatch):
     monkeypatch.setattr(K, "select_queries", _select)
     monkeypatch.setattr(K, "conv3x3_layernorm", _conv3x3_ln)
     monkeypatch.setattr(K, "window_merge_layernorm", _window_merge)
+    monkeypatch.setattr(K, "window_partition_layernorm", _window_partition)
     monkeypatch.setattr(K, "status_word", lambda *a: None)
     w = random_weights(0)
 

@@ -195,3 +195,63 @@ extern "C" int ko_deform_attn(const float* value, const float* loc, const float*
     deform_scalar_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(value, loc, aw, s, out);
   return ko::check_launch("ko_deform_attn");
 }
+
+// ---------------------------------------------------------------------------------------------------------
+// Sampling locations and point weights from the cross-attention's projection (ko_deform_prep).
+// Semantics: fast_rfdetr/model.py:222-225 —
+//   off = oa[..., :NH*NP*2] as [NH][NP][2],   aw = softmax over points of oa[..., NH*NP*2:] as [NH][NP],
+//   loc = ref_xy + off / NP * ref_wh * 0.5   (the same fp32 operations in the same order as the reference,
+//   so loc is bit-identical to it; the softmax is max-subtracted with expf).
+// One thread per (frame, query, head); replaces the softmax and the four elementwise launches per layer.
+// ---------------------------------------------------------------------------------------------------------
+namespace {
+
+constexpr int kPrepMaxPoints = 8;
+
+__global__ void __launch_bounds__(256) deform_prep_kernel(const float* __restrict__ oa,
+                                                          const float* __restrict__ ref, int64_t rows, int NH,
+                                                          int NP, int64_t ld_oa, float* __restrict__ loc,
+                                                          float* __restrict__ aw) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= rows * NH) return;
+  const int64_t r = t / NH;  // (frame, query) row
+  const int h = static_cast<int>(t - r * NH);
+  const float* o = oa + r * ld_oa;
+  const float4 rb = reinterpret_cast<const float4*>(ref)[r];
+  const float np = static_cast<float>(NP);
+  float* lp = loc + t * NP * 2;
+  for (int p = 0; p < NP; ++p) {
+    const float ox = o[(h * NP + p) * 2], oy = o[(h * NP + p) * 2 + 1];
+    lp[2 * p] = rb.x + ox / np * rb.z * 0.5f;
+    lp[2 * p + 1] = rb.y + oy / np * rb.w * 0.5f;
+  }
+  const float* lg = o + NH * NP * 2 + h * NP;
+  float e[kPrepMaxPoints];
+  float mx = lg[0];
+  for (int p = 1; p < NP; ++p) mx = fmaxf(mx, lg[p]);
+  float sum = 0.f;
+  for (int p = 0; p < NP; ++p) {
+    e[p] = expf(lg[p] - mx);
+    sum += e[p];
+  }
+  for (int p = 0; p < NP; ++p) aw[t * NP + p] = e[p] / sum;
+}
+
+}  // namespace
+
+extern "C" int ko_deform_prep(const float* oa, const float* ref, int64_t B, int64_t NQ, int64_t NH, int64_t NP,
+                              int64_t ld_oa, float* loc, float* aw, ko_stream_t stream) {
+  const char* who = "ko_deform_prep";
+  if (B < 0 || NQ < 0 || NH < 1 || NP < 1 || NP > kPrepMaxPoints || ld_oa < NH * NP * 3)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT,
+                    std::string(who) + ": need 1 <= NP <= 8 points and a row of at least NH * NP * 3 values");
+  const int64_t rows = B * NQ;
+  if (rows == 0) return KO_OK;
+  if (!oa || !ref || !loc || !aw) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": null pointer");
+  if (!ko::aligned16(ref)) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": ref must be 16-byte aligned");
+  const int64_t blocks = (rows * NH + 255) / 256;
+  if (blocks > 0x7fffffff) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": too many rows");
+  deform_prep_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      oa, ref, rows, static_cast<int>(NH), static_cast<int>(NP), ld_oa, loc, aw);
+  return ko::check_launch(who);
+}

@@ -242,6 +242,21 @@ def deform_attn(value, loc, aw, grid_hw, nh, hd, offset=0):
     return out
 
 
+def deform_prep(oa, ref, nh, npts):
+    """oa [B, NQ, >= NH*NP*3] (sampling offsets, then attention logits), ref [B, NQ, 4] -> (loc [B, NQ, NH, NP, 2],
+    aw [B, NQ, NH, NP]): the location arithmetic and point softmax of model.py:222-225 in one launch."""
+    _need(oa, "oa")
+    _need(ref, "ref")
+    b, nq, w = oa.shape
+    if tuple(ref.shape) != (b, nq, 4) or w < nh * npts * 3:
+        raise ValueError("deform_prep: oa must be [B, NQ, >= NH*NP*3] and ref [B, NQ, 4]")
+    loc = torch.empty((b, nq, nh, npts, 2), dtype=torch.float32, device=oa.device)
+    aw = torch.empty((b, nq, nh, npts), dtype=torch.float32, device=oa.device)
+    call("ko_deform_prep", oa.data_ptr(), ref.data_ptr(), b, nq, nh, npts, w, loc.data_ptr(), aw.data_ptr(),
+         _stream())
+    return loc, aw
+
+
 # ---- multi-head attention ----
 def attention(q, k, v, heads, scale, out=None):
     """softmax(scale * q k^T) v for every head, fp32 grade (the 3xTF32 tcgen05 flash kernel; the reference uses

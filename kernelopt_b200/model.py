@@ -279,10 +279,7 @@ class RFDETR:
             o = K.attention(qk[..., :D_MODEL], qk[..., D_MODEL:], v, SA_HEADS, 1 / math.sqrt(hd))
             _, tgt = lyr["out"].ln(o, lyr["norm1"], resid=tgt, write_h=False)                  # LN(tgt + out(o))
             oa = lyr["offaw"](tgt + qpos)                                                         # [B, 300, 96]
-            off = oa[..., :CA_HEADS * CA_POINTS * 2].reshape(b, N_QUERIES, CA_HEADS, CA_POINTS, 2)
-            aw = torch.softmax(oa[..., CA_HEADS * CA_POINTS * 2:].reshape(b, N_QUERIES, CA_HEADS, CA_POINTS), -1)
-            r = ref[:, :, None, None, :]
-            loc = r[..., :2] + off / CA_POINTS * r[..., 2:] * 0.5
+            loc, aw = K.deform_prep(oa, ref.contiguous(), CA_HEADS, CA_POINTS)  # locations + point softmax
             s = K.deform_attn(values, loc, aw, (GRID, GRID), CA_HEADS, D_MODEL // CA_HEADS, offset=i * D_MODEL)
             _, tgt = lyr["oproj"].ln(s, lyr["norm2"], resid=tgt, write_h=False)
             _, tgt = lyr["l2"].ln(lyr["l1"](tgt, "relu"), lyr["norm3"], resid=tgt, write_h=False)

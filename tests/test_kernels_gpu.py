@@ -277,6 +277,32 @@ def deform_inputs(r, b, row=256, nq=300, nh=16, npts=2):
     return value, loc, aw
 
 
+@pytest.mark.parametrize("b,nq,nh,npts,width", [(2, 300, 16, 2, 96), (3, 37, 4, 4, 50), (1, 1, 1, 1, 3)])
+def test_deform_prep(cuda, b, nq, nh, npts, width):
+    """ko_deform_prep: loc bit-identical to the reference's float32 arithmetic (model.py:224-225), aw = the point
+    softmax within 1e-6."""
+    g = torch.Generator().manual_seed(b * 100 + nq)
+    oa = (2 * torch.randn(b, nq, width, generator=g)).to(cuda)
+    ref = torch.cat([torch.rand(b, nq, 2, generator=g), 0.05 + 0.3 * torch.rand(b, nq, 2, generator=g)], -1).to(cuda)
+    loc, aw = K.deform_prep(oa, ref, nh, npts)
+    off = oa[..., :nh * npts * 2].reshape(b, nq, nh, npts, 2)
+    r = ref[:, :, None, None, :]
+    want_loc = r[..., :2] + off / npts * r[..., 2:] * 0.5
+    lg = oa[..., nh * npts * 2:nh * npts * 3].reshape(b, nq, nh, npts).double()
+    want_aw = torch.softmax(lg, -1)
+    torch.cuda.synchronize()
+    assert torch.equal(loc, want_loc)
+    assert (aw.double() - want_aw).abs().max().item() <= 1e-6
+
+
+def test_deform_prep_rejects_bad_sizes(cuda):
+    oa, ref = torch.zeros(1, 4, 40, device=cuda), torch.zeros(1, 4, 4, device=cuda)
+    with pytest.raises(ValueError):  # the row holds fewer than NH * NP * 3 values
+        K.deform_prep(oa, ref, 16, 2)
+    with pytest.raises(ValueError):  # more than 8 points (checked by the entry point)
+        K.deform_prep(torch.zeros(1, 4, 27, device=cuda), ref, 1, 9)
+
+
 @pytest.mark.parametrize("batch", [1, 3, 64])
 def test_deform_attn(cuda, batch):
     r = np.random.default_rng(batch + 11)

@@ -93,6 +93,14 @@ def _window_partition(t, pos, cls, win, gamma, beta, eps=1e-6, h=None, y=None):
     return hh, F.layer_norm(hh, (c,), gamma, beta, eps)
 
 
+def _deform_prep(oa, ref, nh, npts):
+    b, nq, _ = oa.shape
+    off = oa[..., :nh * npts * 2].reshape(b, nq, nh, npts, 2)
+    aw = torch.softmax(oa[..., nh * npts * 2:nh * npts * 3].reshape(b, nq, nh, npts), -1)
+    r = ref[:, :, None, None, :]
+    return r[..., :2] + off / npts * r[..., 2:] * 0.5, aw
+
+
 def _im2col3x3(x, out=None):
     b, h, w, c = x.shape
     xp = F.pad(x, (0, 0, 1, 1, 1, 1))
@@ -115,6 +123,7 @@ def cpu_model(monkeypatch):
     monkeypatch.setattr(K, "conv3x3_layernorm", _conv3x3_ln)
     monkeypatch.setattr(K, "window_merge_layernorm", _window_merge)
     monkeypatch.setattr(K, "window_partition_layernorm", _window_partition)
+    monkeypatch.setattr(K, "deform_prep", _deform_prep)
     monkeypatch.setattr(K, "status_word", lambda *a: None)
     w = random_weights(0)
 

@@ -1045,7 +1045,15 @@ extern "C" int ko_linear_residual_ln_f32_packed(const float* x, const float* w_p
     return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": y must not alias x, resid or h_out");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool split = K > 512;
-  const int bn = N == 384 ? 192 : N == 512 ? 256 : static_cast<int>(N);
+  // N = 256 rows fit one 256-wide CTA or a cluster of two 128-wide ones. With fewer row blocks than two per SM
+  // (the decoder's 300 queries per frame), the pair halves each row block's time and wins (fc2, K = 2048: 225 ->
+  // 196 us at 64 frames); with many row blocks the single CTA keeps its wider tile (158 against 185 us at 102400
+  // rows, K = 384).
+  const int64_t m_tiles = (M + BM - 1) / BM;
+  const int bn = N == 384 ? 192
+                 : N == 512 ? 256
+                 : (N == 256 && m_tiles < 2 * static_cast<int64_t>(ko::device_info().sm_count)) ? 128
+                                                                                                : static_cast<int>(N);
 #define KO_LN_CASE(BNV)                                                                                         \
   if (bn == BNV)                                                                                               \
     return split ? launch_gemm_ln<BNV, true>(x, w_packed, bias, scale, resid, gamma, beta, eps, M, K, N, act,   \

@@ -57,8 +57,10 @@ def run(cuda, d, eps=1e-6, act=None, in_place=False, write_h=True):
 
 @pytest.mark.parametrize("m,k,n", [(3208, 384, 384), (3208, 1536, 384), (102656 // 8, 384, 384), (1, 384, 384),
                                    (129, 1536, 384), (2400, 256, 256), (2400, 2048, 256), (1000, 320, 192),
-                                   (777, 512, 512), (130, 640, 128)])
+                                   (777, 512, 512), (130, 640, 128), (40000, 384, 256)])
 def test_linear_residual_ln(cuda, m, k, n):
+    # N = 256 runs as a cluster of two 128-wide CTAs below two row blocks per SM (2400 rows) and as one
+    # 256-wide CTA above (40000 rows).
     d = make(m, k, n, m + k + n)
     h_out, y = run(cuda, d)
     rh, ry = OK.linear_residual_layernorm(d["x"], d["w"], d["bias"], d["scale"], d["resid"], d["gamma"], d["beta"],

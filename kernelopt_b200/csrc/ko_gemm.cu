@@ -138,8 +138,20 @@ struct TileSched {
   __device__ int n0(int tile, int bn) const { return (tile % n_tiles) * bn + col0; }
 };
 
+// erf(x) by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26 (rational approximation
+// in t = 1 / (1 + p|x|) times exp(-x^2); absolute error below 1.5e-7 over the whole real line).
+__device__ __forceinline__ float erf_as7126(float x) {
+  const float ax = fabsf(x);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, ax, 1.0f));
+  const float poly =
+      t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-ax * ax * 1.4426950408889634f));
+  return copysignf(1.0f - poly * e, x);
+}
+
 __device__ __forceinline__ float apply_act(float v, int act) {
-  if (act == KO_ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
+  if (act == KO_ACT_GELU) return 0.5f * v * (1.0f + erf_as7126(v * 0.7071067811865476f));
   if (act == KO_ACT_RELU) return fmaxf(v, 0.0f);
   return v;
 }

@@ -138,20 +138,23 @@ struct TileSched {
   __device__ int n0(int tile, int bn) const { return (tile % n_tiles) * bn + col0; }
 };
 
-// erf(x) by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26 (rational approximation
-// in t = 1 / (1 + p|x|) times exp(-x^2); absolute error below 1.5e-7 over the whole real line).
-__device__ __forceinline__ float erf_as7126(float x) {
-  const float ax = fabsf(x);
-  const float t = __fdividef(1.0f, fmaf(0.3275911f, ax, 1.0f));
-  const float poly =
-      t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
-  float e;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-ax * ax * 1.4426950408889634f));
-  return copysignf(1.0f - poly * e, x);
+// GELU(v) = v * Phi(v), Phi the standard normal CDF = (1 + erf(v / sqrt 2)) / 2, with erfc(x) for x >= 0 from
+// Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26: erfc(x) = t (a1 + t (a2 + ... + t a5))
+// exp(-x^2), t = 1 / (1 + p x), absolute error below 1.5e-7. With x = |v| / sqrt 2 and q = erfc(x) / 2 (the
+// factors 1/sqrt 2 and 1/2 folded into p and the a_i): Phi(v) = 1 - q for v >= 0 and q for v < 0.
+__device__ __forceinline__ float gelu_as7126(float v) {
+  const float ax = fabsf(v);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f * 0.7071067811865476f, ax, 1.0f));
+  const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 0.5f * 1.061405429f, 0.5f * -1.453152027f),
+                                               0.5f * 1.421413741f), 0.5f * -0.284496736f), 0.5f * 0.254829592f);
+  float e;  // exp(-v^2 / 2) as 2^(-v^2 log2(e) / 2)
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(v * v * -0.7213475204444817f));
+  const float vq = v * (poly * e);
+  return v >= 0.0f ? v - vq : vq;
 }
 
 __device__ __forceinline__ float apply_act(float v, int act) {
-  if (act == KO_ACT_GELU) return 0.5f * v * (1.0f + erf_as7126(v * 0.7071067811865476f));
+  if (act == KO_ACT_GELU) return gelu_as7126(v);
   if (act == KO_ACT_RELU) return fmaxf(v, 0.0f);
   return v;
 }

@@ -58,7 +58,7 @@ constexpr int EPI_LN = 1;
 // (mean, M2) lands in [2][128] float2; two mbarriers count the peer's arrivals, four (one per lane quadrant)
 // the two warps of a pair, and eight (one per epilogue warp) the TMA loads into the warps' staging tiles.
 constexpr uint32_t kLnStatBytes = 2 * 2 * 128 * 8 + 2 * 128 * 8 + 2 * 8 + 4 * 8 + 8 * 8;
-constexpr uint32_t kLnStatRegion = 6400;
+constexpr uint32_t kLnStatRegion = 6400 + 4 * 256 * 4;  // + the CTA's column slice of bias, scale, gamma, beta
 static_assert(kLnStatBytes <= kLnStatRegion, "stat region");
 
 template <int BN, int BKB, bool SPLIT, int EPI = EPI_ACT>
@@ -228,6 +228,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* peer_bar = reinterpret_cast<uint64_t*>(peer_stats + 2 * 128);
   uint64_t* pair_bar = peer_bar + 2;
   uint64_t* load_bar = pair_bar + 4;
+  // EPI_LN: the CTA's BN columns never change (tiles are row blocks), so their bias, scale (1 when absent),
+  // gamma and beta are read from global memory once, here, and by the epilogue from shared memory
+  float* ln_par = reinterpret_cast<float*>(store_smem + kStoreBytes + 256 + 6400);  // [4][BN]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const TileSched<EPI> ts(args, BN);
@@ -266,6 +269,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
+  }
+  if (EPI == EPI_LN) {
+    for (int i = threadIdx.x; i < BN; i += blockDim.x) {
+      const int col = ts.col0 + i;
+      ln_par[i] = args.bias ? args.bias[col] : 0.f;
+      ln_par[BN + i] = args.scale ? args.scale[col] : 1.f;
+      ln_par[2 * BN + i] = args.gamma[col];
+      ln_par[3 * BN + i] = args.beta[col];
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -590,10 +602,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col = col0 + 4 * j;
           float4* slot = reinterpret_cast<float4*>(stile + lane * 128 + ((j ^ (lane & 7)) << 4));
           const float4 hv = args.resid ? *slot : make_float4(0.f, 0.f, 0.f, 0.f);
-          const float4 b = args.bias ? __ldg(reinterpret_cast<const float4*>(args.bias + col))
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-          const float4 sc = args.scale ? __ldg(reinterpret_cast<const float4*>(args.scale + col))
-                                       : make_float4(1.f, 1.f, 1.f, 1.f);
+          const float4 b = *reinterpret_cast<const float4*>(ln_par + (col - ts.col0));
+          const float4 sc = *reinterpret_cast<const float4*>(ln_par + BN + (col - ts.col0));
           float4 v;
           v.x = hv.x + (__uint_as_float(r[4 * j + 0]) + b.x) * sc.x;
           v.y = hv.y + (__uint_as_float(r[4 * j + 1]) + b.y) * sc.y;
@@ -688,8 +698,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int col = col0 + 4 * j;
-          const float4 g = __ldg(reinterpret_cast<const float4*>(args.gamma + col));
-          const float4 bt = __ldg(reinterpret_cast<const float4*>(args.beta + col));
+          const float4 g = *reinterpret_cast<const float4*>(ln_par + 2 * BN + (col - ts.col0));
+          const float4 bt = *reinterpret_cast<const float4*>(ln_par + 3 * BN + (col - ts.col0));
           float4 o;
           o.x = ln_act((__uint_as_float(r[4 * j + 0]) - mean) * rstd * g.x + bt.x, args.act);
           o.y = ln_act((__uint_as_float(r[4 * j + 1]) - mean) * rstd * g.y + bt.y, args.act);

@@ -35,12 +35,12 @@ WORKLOAD = ("RF-DETR-Medium fp32 inference on seeded 1920x1080 uint8 BGR frames:
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per plain GEMM launch (gemm_tf32x3_kernel with the
-# bias / activation epilogue), mean over the 70 such launches of one step at 64 frames, from one ncu capture:
+# bias / activation epilogue), mean over the 50 such launches of one step at 64 frames, from one ncu capture:
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --cache-control none
 #       --clock-control none -k regex:gemm_tf32x3 -c 95 python bench.py --steps 1 --warmup 3 --no-cpu-baseline
-# (the first 95 launches matching the pattern are the step's 70 plain and 25 LayerNorm-epilogue GEMMs; the plain
-# ones total 34 076 MB against 33 864 MB of algorithmic bytes: x, the output and the split weight once each).
-GEMM_TRAFFIC_PER_LAUNCH = {64: 486.8e6}
+# (the first 95 launches matching the pattern are one forward's 50 plain and 45 LayerNorm-epilogue GEMMs; the plain
+# ones total 19 125 MB against 20 089 MB of algorithmic bytes: x, the output and the split weight once each).
+GEMM_TRAFFIC_PER_LAUNCH = {64: 382.5e6}
 
 
 def frames_for(rank: int, n: int) -> np.ndarray:

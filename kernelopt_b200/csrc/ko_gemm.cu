@@ -149,8 +149,11 @@ __device__ __forceinline__ float gelu_as7126(float v) {
                                                0.5f * 1.421413741f), 0.5f * -0.284496736f), 0.5f * 0.254829592f);
   float e;  // exp(-v^2 / 2) as 2^(-v^2 log2(e) / 2)
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(v * v * -0.7213475204444817f));
-  const float vq = v * (poly * e);
-  return v >= 0.0f ? v - vq : vq;
+  const float q = poly * e;
+  const float vq = v * q;
+  // q underflows to 0 for large |v|: GELU(v) = v there (+inf included, where v * q would be inf * 0), and
+  // v * q keeps -inf -> NaN, as 0.5 * v * (1 + erf(v / sqrt 2)) gives
+  return v >= 0.0f ? (q > 0.0f ? v - vq : v) : vq;
 }
 
 __device__ __forceinline__ float apply_act(float v, int act) {

@@ -9,6 +9,8 @@ Tolerances:
 """
 from __future__ import annotations
 
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -369,6 +371,22 @@ def test_linear_gelu_3xtf32(cuda, m, k, n):
     torch.cuda.synchronize()
     K.check_device_status()
     assert_close(g, OK.linear_gelu_f32(x, w, b), what=f"gemm {m}x{k}x{n}")
+
+
+def test_linear_gelu_special_values(cuda):
+    """The GELU epilogue at the ends of its range, as 0.5 * v * (1 + erf(v / sqrt 2)) gives them: +inf -> +inf,
+    -inf -> NaN, large positive v -> v, large negative v -> 0. Powers of two keep the 3xTF32 split exact (lo = 0)."""
+    x = torch.zeros(128, 16)
+    w = torch.zeros(16, 16)
+    x[0, 0], x[1, 0], x[2, 0], x[3, 0], x[4, 0] = 2.0 ** 100, -(2.0 ** 100), 64.0, -64.0, 1.0
+    w[0, 0], w[0, 1] = 2.0 ** 100, 1.0  # column 0: x * 2^100 (overflows to +-inf for rows 0, 1); column 1: x
+    y = K.linear(x.to(cuda), K.pack_weight(w.to(cuda), torch.zeros(16, device=cuda)), "gelu").cpu()
+    assert y[0, 0].item() == float("inf")
+    assert math.isnan(y[1, 0].item())
+    assert y[0, 1].item() == 2.0 ** 100 and y[2, 1].item() == 64.0
+    assert abs(y[1, 1].item()) == 0.0 and abs(y[3, 1].item()) < 1e-30
+    assert abs(y[4, 1].item() - 0.8413447460685429) < 1e-6  # GELU(1) = Phi(1)
+    assert torch.equal(y[5:], torch.zeros(123, 16))
 
 
 @pytest.mark.parametrize("act", [None, "relu"])

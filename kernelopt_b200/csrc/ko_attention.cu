@@ -82,24 +82,12 @@ struct AttnCfg {
   // memory columns and no second CTA waits in tcgen05.alloc.
   static constexpr size_t kSmemNeed = 1024 + kOffBars + 256;
   static constexpr size_t kSmemBytes = kSmemNeed > 120 * 1024 ? kSmemNeed : 120 * 1024;
-  static constexpr int kQChunks = BQ * HD / 4 / kLoadThreads;   // float4 per loader thread for a q tile
-  static constexpr int kKChunks = BKEY * HD / 4 / kLoadThreads;  // ... for a k or v tile
   static_assert(HD == 32 || HD == 64, "head dim 32 or 64");
 };
 
 // Byte offset of 16-byte chunk `c` (0..7) of row `r` in a K-major tile of 128-byte rows, 128-byte swizzle.
 __device__ __forceinline__ uint32_t sw128(int r, int c) {
   return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
-}
-
-// D[tmem] (+)= A[tmem] * B[smem]^T, kind::tf32, one CTA (A: M lanes x K columns of tensor memory).
-__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
 }
 
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }

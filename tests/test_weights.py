@@ -16,7 +16,7 @@ def test_random_weights_schema_and_determinism():
     assert a[W.LAYER.format(11) + "mlp.fc1.weight"].shape == (384, 1536)
     assert a[W.PROJ + "0.m.2.cv2.conv.weight"].shape == (128, 3, 3, 128)
     assert a["proposals"].shape == (1600, 4) and a["proposal_valid"].min() == 1.0
-    assert float(a["_eps." + W.LAYER.format(0) + "norm1.weight"]) == pytest.approx(1e-6)
+    assert float(np.asarray(a["_eps." + W.LAYER.format(0) + "norm1.weight"]).reshape(())) == pytest.approx(1e-6)
     w = a[W.LAYER.format(0) + "mlp.fc2.weight"]
     assert np.abs(w).max() <= 0.04 + 1e-7 and 0.015 < w.std() < 0.02
 

@@ -132,8 +132,12 @@ def window_merge_layernorm(h, grid_hw, win, out, col_off, gamma=None, beta=None,
     b = n // nwin
     if out.dim() != 4 or tuple(out.shape[:3]) != (b, gh, gw):
         raise ValueError(f"out must be [{b}, {gh}, {gw}, channels]")
-    if normalize and (gamma is None or beta is None):
-        raise ValueError("gamma and beta are required to normalize")
+    if normalize:
+        if gamma is None or beta is None:
+            raise ValueError("gamma and beta are required to normalize")
+        for name, t in (("gamma", gamma), ("beta", beta)):
+            if _need(t, name).numel() != c:
+                raise ValueError(f"{name} must have {c} elements")
     call("ko_window_merge_ln", h.data_ptr(), _ptr(gamma), _ptr(beta), float(eps), b, gh, gw, win, c,
          1 if normalize else 0, out.data_ptr(), out.shape[-1], col_off, _stream())
     return out
@@ -150,6 +154,8 @@ def window_partition_layernorm(t, pos, cls, win, gamma, beta, eps=1e-6, h=None, 
     b, gh, gw, c = t.shape
     if tuple(pos.shape) != (gh, gw, c) or cls.numel() != c:
         raise ValueError("pos must be [H, W, C] and cls [C]")
+    if gamma.numel() != c or beta.numel() != c:
+        raise ValueError(f"gamma and beta must have {c} elements")
     if gh % win or gw % win:
         raise ValueError("H and W must be multiples of win")
     shape = (b * (gh // win) * (gw // win), 1 + win * win, c)

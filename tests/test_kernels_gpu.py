@@ -243,6 +243,8 @@ def test_window_partition_rejects_bad_shapes(cuda):
         K.window_partition_layernorm(t, pos, cls, 3, g, g)
     with pytest.raises(ValueError):  # pos of the wrong grid
         K.window_partition_layernorm(t, pos[:4], cls, 4, g, g)
+    with pytest.raises(ValueError):  # gamma shorter than C
+        K.window_partition_layernorm(t, pos, cls, 4, g[:32].contiguous(), g)
     with pytest.raises(ValueError):  # C not a multiple of 4 (checked by the entry point)
         K.window_partition_layernorm(t[..., :62].contiguous(), pos[..., :62].contiguous(), cls[:62].contiguous(), 4,
                                      g[:62].contiguous(), g[:62].contiguous())
@@ -257,6 +259,9 @@ def test_window_merge_rejects_bad_shapes(cuda):
         K.window_merge_layernorm(h, (8, 8), 3, out, 0, normalize=False)
     with pytest.raises(ValueError):  # normalize without gamma/beta
         K.window_merge_layernorm(h, (8, 8), 4, out, 0)
+    g = torch.ones(32, device=cuda)
+    with pytest.raises(ValueError):  # gamma / beta shorter than C
+        K.window_merge_layernorm(h, (8, 8), 4, out, 0, g, g)
 
 
 @pytest.mark.parametrize("shape", [(2, 7, 9, 12), (4, 40, 40, 128)])

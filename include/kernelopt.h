@@ -159,8 +159,8 @@ int ko_deform_attn(const float* value, const float* loc, const float* aw, int64_
 /* The sampling inputs of one decoder cross-attention layer from its projection: oa: float32 [B*NQ rows][ld_oa]
  * holding NH*NP*2 sampling offsets (head, point, x/y) then NH*NP attention logits (head, point); ref: float32
  * [B*NQ][4] (cx, cy, w, h), 16-byte aligned. Writes loc: [B*NQ][NH][NP][2] = ref_xy + off / NP * ref_wh * 0.5 and
- * aw: [B*NQ][NH][NP] = softmax over the points of the logits. NP <= 8. Replaces the reshape / softmax / location
- * arithmetic of fast_rfdetr/model.py:222-225 with one launch. */
+ * aw: [B*NQ][NH][NP] = softmax over the points of the logits. NP <= 8, NH <= 4096. Replaces the reshape /
+ * softmax / location arithmetic of fast_rfdetr/model.py:222-225 with one launch. */
 int ko_deform_prep(const float* oa, const float* ref, int64_t B, int64_t NQ, int64_t NH, int64_t NP, int64_t ld_oa,
                    float* loc, float* aw, ko_stream_t stream);
 

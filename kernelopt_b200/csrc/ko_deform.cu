@@ -242,9 +242,9 @@ __global__ void __launch_bounds__(256) deform_prep_kernel(const float* __restric
 extern "C" int ko_deform_prep(const float* oa, const float* ref, int64_t B, int64_t NQ, int64_t NH, int64_t NP,
                               int64_t ld_oa, float* loc, float* aw, ko_stream_t stream) {
   const char* who = "ko_deform_prep";
-  if (B < 0 || NQ < 0 || NH < 1 || NP < 1 || NP > kPrepMaxPoints || ld_oa < NH * NP * 3)
-    return ko::fail(KO_ERR_INVALID_ARGUMENT,
-                    std::string(who) + ": need 1 <= NP <= 8 points and a row of at least NH * NP * 3 values");
+  if (B < 0 || NQ < 0 || NH < 1 || NH > 4096 || NP < 1 || NP > kPrepMaxPoints || ld_oa < NH * NP * 3)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": need 1 <= NH <= 4096 heads, 1 <= NP <= 8 points "
+                                                                "and a row of at least NH * NP * 3 values");
   const int64_t rows = B * NQ;
   if (rows == 0) return KO_OK;
   if (!oa || !ref || !loc || !aw) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": null pointer");

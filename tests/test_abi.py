@@ -42,6 +42,33 @@ def test_abi_version_and_error_string():
     ("ko_linear_f32_packed", (16, 16, None, 8, 8, 8, 7, 16, None, None)),                   # unknown act
     ("ko_linear_gelu_f32", (16, 16, 16, 8, 8, 8, 16, 16, 4, None, None)),                   # workspace small
     ("ko_pack_weight_tf32x3", (16, 0, 8, 16, None)),                                        # K = 0
+    ("ko_linear_gelu_f32_noalloc", (16, 16, None, 8, 1 << 20, 1 << 20, 16, None, None)),    # K*N over the scratch
+    ("ko_linear_residual_ln_f32_packed",
+     (16, 16, None, None, None, 16, 16, 1e-6, 128, 256, 256, 99, None, 16, None, None)),    # unknown act
+    ("ko_linear_residual_ln_f32_packed",
+     (16, 16, None, None, None, None, None, 1e-6, 128, 256, 256, 0, None, 16, None, None)), # no gamma / beta
+    ("ko_conv3x3_ln_f32_packed", (16, 16, 16, 16, 16, 1e-6, 1, 8, 8, 8, 256, 0, 32, None, None)),   # C % 16 != 0
+    ("ko_conv3x3_ln_f32_packed", (16, 16, 16, 16, 16, 1e-6, 1, 8, 8, 16, 256, 0, 16, None, None)),  # y aliases x
+    ("ko_attention_f32", (16, 16, 16, 16, 1, 128, 1, 48, 0, 48, 0, 48, 0, 48, 0, 48, 0.125, None, None)),  # HD 48
+    ("ko_attention_f32", (16, 16, 16, 16, 1, 128, 1, 32, 0, 30, 0, 32, 0, 32, 0, 32, 0.125, None, None)),  # stride
+    ("ko_layernorm", (16, 16, 16, 1e-6, 10, 6, 0, 16, None)),                                # C % 4 != 0
+    ("ko_layernorm", (16, 16, 16, 1e-6, 10, 8, 1, 16, None)),                                # GELU not offered
+    ("ko_window_merge_ln", (16, 16, 16, 1e-6, 1, 8, 8, 4, 64, 1, 16, 64, 4, None)),          # col_off + C > ldo
+    ("ko_window_merge_ln", (16, None, None, 1e-6, 1, 8, 8, 4, 64, 1, 16, 64, 0, None)),      # normalize, no gamma
+    ("ko_window_partition_ln", (16, 16, 16, 16, 16, 1e-6, 1, 8, 8, 3, 64, 16, 16, None)),    # H % win != 0
+    ("ko_window_partition_ln", (20, 16, 16, 16, 16, 1e-6, 1, 8, 8, 4, 64, 16, 16, None)),    # t unaligned
+    ("ko_deform_prep", (16, 16, 1, 300, 16, 9, 432, 16, 16, None)),                          # NP > 8
+    ("ko_deform_prep", (16, 16, 1, 300, 16, 4, 100, 16, 16, None)),                          # row < NH*NP*3
+    ("ko_deform_prep", (16, 20, 1, 300, 16, 4, 192, 16, 16, None)),                          # ref unaligned
+    ("ko_deform_prep", (16, 16, 1, 300, 1 << 20, 1, 3 << 20, 16, 16, None)),                 # NH > 4096
+    ("ko_select_queries", (16, 16, 16, 16, 16, 1, 100, 2, 300, 16, 16, None)),               # NQ > NP
+    ("ko_select_queries", (16, 16, 16, 16, 16, 1, 5000, 2, 300, 16, 16, None)),              # NP > 4096
+    ("ko_im2col3x3", (16, 1, 8, 8, 6, 16, None)),                                            # C % 4 != 0
+    ("ko_im2col3x3", (20, 1, 8, 8, 8, 16, None)),                                            # x unaligned
+    ("ko_preprocess", (16, 720, 1280, 3840, 16, 16, 16, 2, 640, 0, 16, None)),               # mode 2
+    ("ko_preprocess", (16, 720, 1280, 100, 16, 16, 16, 0, 640, 0, 16, None)),                # stride < 3 W
+    ("ko_preprocess", (16, 720, 1280, 3840, 16, 16, 16, 0, 648, 2, 16, None)),               # PATCH16, dst % 16
+    ("ko_preprocess", (16, 720, 1280, 3840, 16, 16, 16, 0, 640, 5, 16, None)),               # unknown layout
 ])
 def test_invalid_arguments_are_rejected_on_the_host(call):
     name, args = call

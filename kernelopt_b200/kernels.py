@@ -183,14 +183,6 @@ def im2col3x3(x, out=None):
     return out
 
 
-def residual_layernorm_into(h, o, bias, scale, gamma, beta, eps, h_out, y):
-    """In-place variant for preallocated buffers (h_out may be h). No shape checks beyond the C ABI's."""
-    c = h.shape[-1]
-    call("ko_residual_layernorm", h.data_ptr(), o.data_ptr(), _ptr(bias), _ptr(scale), gamma.data_ptr(),
-         beta.data_ptr(), float(eps), h.numel() // c, c, h_out.data_ptr(), y.data_ptr(), _stream())
-    return h_out, y
-
-
 # ---- preprocessing ----
 def preprocess_gpu(img_u8, xtab, ytab, lut, mode, dst=640, layout="hwc", out=None):
     """img_u8: uint8 [H, W, 3] (row-contiguous) CUDA tensor. Returns float32 [dst, dst, 3] normalised RGB

@@ -7,10 +7,14 @@
 plus attention(q, k, v, heads, scale), which replaces the reference's mx.fast.scaled_dot_product_attention calls.
 
 Every call goes to libkernelopt.so (hand-written sm_100a CUDA) on the caller's current CUDA stream. Outputs
-are freshly allocated; inputs are read-only and must be contiguous float32 (uint8/int32 for preprocessing)
-CUDA tensors. There is no CPU path: CPU tensors raise ValueError, a missing library raises RuntimeError.
-Beyond the reference's API: batched preprocessing (`preprocess_batch`) and the pre-split weight form of the
-GEMM (`pack_weight` / `linear`), which the model uses for every dense layer.
+are freshly allocated unless the function takes an `out` (or `h` / `y`) buffer; inputs are read-only and must be
+contiguous float32 (uint8/int32 for preprocessing) CUDA tensors. There is no CPU path: CPU tensors raise
+ValueError, a missing library raises RuntimeError.
+Beyond the reference's API, the model's other fused steps: batched preprocessing (`preprocess_batch`); the
+pre-split weight form of the GEMM (`pack_weight` / `linear`) used for every dense layer, with its residual +
+LayerNorm epilogue (`linear_residual_layernorm`) and the implicit 3x3 convolution (`conv3x3_layernorm`);
+`layernorm`, `im2col3x3`; the backbone's `window_partition_layernorm` / `window_merge_layernorm`; the decoder's
+`select_queries` and `deform_prep`.
 """
 from __future__ import annotations
 

@@ -8,13 +8,17 @@ Call sites of the reference's kernels (model.py:122, 125, 131, 226) use the same
                        encoder-output linear + LN run through the same fused kernel
   linear_gelu_f32      backbone fc1 (the 3xTF32 tcgen05 GEMM with the GELU epilogue)
   deform_attn          decoder cross-attention sampling, on the one fused [B,1600,1024] value projection
-Every other dense layer (QKV, out-proj, fc2, the patch embedding, the projector's 1x1 and im2col'd 3x3 convs,
-the decoder linears) runs on the same fp32-grade tcgen05 GEMM; only the layers whose output width is not a
+Every other dense layer (QKV, out-proj, fc2, the patch embedding, the projector's 1x1 convs, the decoder
+linears) runs on the same fp32-grade tcgen05 GEMM. The projector's 3x3 convs run on it as an implicit GEMM with
+LayerNorm + SiLU in the epilogue (im2col + GEMM for other widths). Only the layers whose output width is not a
 multiple of 4 (11 classes, 4 box coordinates) use torch's fp32 matmul. Attention — the backbone's windowed and
 global self-attention and the decoder's self-attention (the reference's mx.fast.scaled_dot_product_attention) — runs
-on the fp32-grade 3xTF32 tcgen05 flash-attention kernel, straight on column slices of the fused QKV projection.
-The remaining LayerNorms run on the LayerNorm kernel; the top-300 query selection is one kernel; softmax is a torch
-op in fp32 with TF32 disabled.
+on the fp32-grade 3xTF32 tcgen05 flash-attention kernel, straight on column slices of the fused QKV projection,
+softmax included. The backbone's entry (pos add, windows, class token, first LayerNorm) and each tapped layer's
+merge + LayerNorm are one kernel each. LayerNorms not fused into a GEMM run on the LayerNorm kernel. The top-300
+query selection is one kernel, and so is the sampler's input step (locations + point softmax). What stays in torch
+is glue (the sine embedding of the query boxes, tgt + qpos, the heads' narrow outputs), in fp32 with TF32
+disabled.
 
 The input is the patch layout the preprocessing kernel writes (PATCH16: [B, 1600, 768]), which makes the
 16x16/16 patch-embedding convolution one GEMM; NHWC [B, 640, 640, 3] (the reference's input) is accepted too.

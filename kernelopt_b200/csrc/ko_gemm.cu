@@ -21,7 +21,14 @@
 //               alternate k-blocks
 //   warps 10-17 epilogue: TMEM -> registers (tcgen05.ld), + bias, activation, a swizzled 32x32 tile in shared
 //               memory per warp, TMA store (two warps per TMEM lane quadrant)
-// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the MMAs of tile i+1.
+// Two TMEM accumulators let the epilogue of tile i overlap the MMAs of tile i+1 (one, where the correction
+// accumulator of SPLIT, below, leaves no room for a second).
+// Two more forms share this kernel:
+//   * the LayerNorm epilogue (EPI_LN): out-projection / fc2 / conv + bias, * layer scale, + residual, then a
+//     LayerNorm over whole rows; rows wider than one tile are split over a cluster of two CTAs that swap
+//     their row statistics through distributed shared memory;
+//   * the implicit 3x3 convolution (conv_c > 0): each k-block is one tap's channel slice, loaded by TMA from
+//     the image rows shifted by that tap; the split warps zero the rows whose shifted pixel is padding.
 // Every wait on an mbarrier is bounded (2 s); on timeout the CTA stops, drains what it issued, frees TMEM and
 // reports KO_ERR_DEVICE_TIMEOUT through dev_status.
 #include <algorithm>

@@ -16,6 +16,8 @@
 // of the map in shared memory, one CTA per (frame, head), measured slower on B200: 45 us against 31 us at
 // 64 frames — two such CTAs per SM alternate between copying and sampling instead of overlapping many gathers.)
 // A scalar kernel covers head sizes or column offsets that are not multiples of 4.
+// ko_deform_prep builds the sampler's inputs from the merged offset / logit projection: the sampling locations
+// and the softmax over each head's points (model.py:222-225), one thread per (frame, query, head).
 #include "ko_common.cuh"
 
 namespace {

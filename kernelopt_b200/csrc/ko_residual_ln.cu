@@ -21,6 +21,9 @@ __device__ __forceinline__ float apply_act(float r, int act) {
 
 // RESID: h_out = h + (o + bias) * scale is normalised (and written); otherwise h itself is normalised and h_out is
 // not written (plain LayerNorm). ACT: KO_ACT_NONE or KO_ACT_SILU on the normalised output.
+// The backbone's window entry (ko_window_partition_ln: pos add, window partition, class token, first LayerNorm)
+// and window merge (ko_window_merge_ln: final LayerNorm of a tapped layer into its channel slice of the projector
+// input) use the same one-warp-per-row scheme, with the row's source or destination remapped.
 template <int V, bool RESID>
 __global__ void __launch_bounds__(32 * kRowsPerBlock) residual_ln_kernel(
     const float* h, const float* __restrict__ o, const float* __restrict__ bias, const float* __restrict__ scale,

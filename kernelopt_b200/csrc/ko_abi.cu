@@ -1,7 +1,7 @@
 // Status reporting, device checks and tensor-map encoding shared by all entry points of libkernelopt.
 #include <cstdio>
 #include <mutex>
-#include <vector>
+#include <string>
 
 #include "ko_common.cuh"
 
@@ -25,19 +25,25 @@ int check_launch(const char* what) {
   return KO_OK;
 }
 
+// One slot per device in a fixed array: callers keep the returned reference after the lock is released, while
+// threads driving other devices may fill their own slots, so the storage must never move. A slot is written once,
+// under the lock, after all four attributes were read; until then it reads as zeros.
 const DeviceInfo& device_info() {
+  constexpr int kMaxDevices = 64;
   static std::mutex mu;
-  static std::vector<DeviceInfo> cache;
+  static DeviceInfo cache[kMaxDevices];
+  static const DeviceInfo none;
   int dev = 0;
-  cudaGetDevice(&dev);
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return none;
   std::lock_guard<std::mutex> lock(mu);
-  if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1);
   DeviceInfo& d = cache[dev];
   if (d.sm_count == 0) {
-    cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
-    cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
-    cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
+    DeviceInfo q;
+    if (cudaDeviceGetAttribute(&q.sm_count, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&q.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&q.major, cudaDevAttrComputeCapabilityMajor, dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&q.minor, cudaDevAttrComputeCapabilityMinor, dev) == cudaSuccess && q.sm_count > 0)
+      d = q;
   }
   return d;
 }

@@ -87,3 +87,14 @@ def test_preprocess_batch_rejects_empty_and_oversized():
 
 def test_linear_workspace_size():
     assert _lib.lib().ko_linear_workspace_bytes(384, 1536) == 2 * 384 * 1536 * 4
+
+
+def test_check_device_reports_a_missing_gpu():
+    """Without a CUDA device the device check fails cleanly (KO_ERR_UNSUPPORTED and a message) on every call."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    for _ in range(2):
+        assert _lib.lib().ko_check_device() == _lib.KO_ERR_UNSUPPORTED
+        assert b"sm_100a" in _lib.lib().ko_last_error_string()

@@ -109,6 +109,9 @@ class FastBasketballDetector:
             self.model = RFDETR(load_weights(model_path, cache_dir), self.device)
             lut = (np.arange(256, dtype=np.float32)[:, None] / 255. - MEAN) / STD   # same float32 ops as Ballform
             self._lut = torch.from_numpy(np.ascontiguousarray(lut.T)).to(self.device)
+            # The weight splits were launched on this thread's current stream; the instance's own stream is
+            # non-blocking and would not wait for them.
+            torch.cuda.current_stream(self.device).synchronize()
             self.stream = torch.cuda.Stream(self.device)
         self._tables: dict[tuple[int, int], tuple[int, torch.Tensor, torch.Tensor]] = {}
         self._runners: dict[int, _GraphRunner] = {}

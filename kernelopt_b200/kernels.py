@@ -413,7 +413,8 @@ _pack_lock = threading.Lock()
 def linear_gelu_f32(x, w, bias):
     """GELU(x @ w + bias) for float32 x [..., K], w [K, N], bias [N] (kernels.py:271-285).
 
-    The split of w is cached per weight tensor (and redone if the tensor is modified in place)."""
+    The split of w is cached per weight tensor (and redone if the tensor is modified in place). A new split is
+    complete before it enters the cache, so callers on other streams can use it at once (outside graph capture)."""
     _need(x, "x")
     _need(w, "w")
     _need(bias, "bias")
@@ -421,6 +422,8 @@ def linear_gelu_f32(x, w, bias):
         hit = _pack_cache.get(w)
         if hit is None or hit[0] != w._version:
             hit = (w._version, PackedWeight(w))
+            if not torch.cuda.is_current_stream_capturing():
+                torch.cuda.current_stream().synchronize()
             _pack_cache[w] = hit
     pw = hit[1]
     m = x.numel() // pw.k

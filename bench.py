@@ -12,6 +12,10 @@ CUDA-event time of K steps. `value` has the frames already resident in HBM (the 
 ~B x 60 MB of activations — is far larger than the 126 MB L2, so no flush is needed); `e2e` runs the same
 steps through FastBasketballDetector.detect_stream from pinned host frames, with every step's H2D copy of its
 frames and D2H copy of its outputs inside the timed region (pipelined: step i+1's copy-in overlaps step i).
+`stream` runs the full-forward config's 512-frame stream as stated: split over the N ranks
+(stream.run_sharded_stream), from pinned host frames, with the outputs gathered to the host of rank 0 in stream
+order inside the timed region (total work fixed: strong scaling). Both arms preprocess with OpenCV's
+fixed-point arithmetic (resize_policy="opencv"), which is bit-exact with the x86-64 cv2.resize the CPU arm calls.
 
 --impl reference times the reference's CPU path on the host cores instead: cv2.resize + numpy normalisation and
 the reference's unfused RF-DETR graph restated in torch-CPU fp32 (the oracle; MLX itself cannot be installed
@@ -189,7 +193,8 @@ def run_ours(args, rank: int, world: int):
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=300))
     B = args.batch
-    det = FastBasketballDetector("random:0", warmup_batch_sizes=(), device=dev)
+    # "opencv": the same resize arithmetic as the CPU arm's x86-64 cv2.resize, so both arms see identical inputs
+    det = FastBasketballDetector("random:0", warmup_batch_sizes=(), device=dev, resize_policy="opencv")
     host = torch.from_numpy(frames_for(rank, B)).pin_memory()
     frames = host.to(dev)
     mode, xt, yt = det._taps(W, H)
@@ -246,6 +251,50 @@ def run_ours(args, rank: int, world: int):
     e2e = world * B * args.steps / e2e_secs
     barrier()
 
+    # ---- the 512-frame stream split over the ranks, gathered in order on rank 0 (strong scaling) ----
+    stream_line = None
+    if args.stream_frames > 0:
+        from kernelopt_b200.stream import run_sharded_stream, shard_range
+
+        def batch_at(s, e):   # the stream's frames cycle through this rank's B pinned frames
+            return host[:e - s]
+
+        def run_stream():
+            if world == 1:
+                outs = list(det.detect_stream(batch_at(s, min(s + B, args.stream_frames))
+                                              for s in range(0, args.stream_frames, B)))
+                return np.concatenate([o[0] for o in outs]), np.concatenate([o[1] for o in outs])
+            return run_sharded_stream(det.detect_stream, batch_at, args.stream_frames, B)
+
+        run_stream()                                            # warm-up (and the gather's first use)
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        res = run_stream()
+        st_secs = max_over_ranks(time.perf_counter() - t0)
+        if rank == 0:
+            assert res[0].shape == (args.stream_frames, 300, 4) and res[1].shape == (args.stream_frames, 300, 11)
+        # the e2e limiter: pinned host -> device copy rate of one batch, all ranks copying at once
+        dev_buf = torch.empty_like(host, device=dev)
+        barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for _ in range(5):
+            dev_buf.copy_(host, non_blocking=True)
+        c1.record()
+        c1.synchronize()
+        h2d_gbs = 5 * host.numel() / (c0.elapsed_time(c1) / 1e3) / 1e9
+        h2d_min = -max_over_ranks(-h2d_gbs)
+        del dev_buf
+        n_mine = len(shard_range(args.stream_frames, rank, world))
+        stream_line = {"frames": args.stream_frames, "value": args.stream_frames / st_secs, "unit": "frames/s",
+                       "seconds": st_secs, "scaling": "strong", "frames_per_rank": n_mine,
+                       "h2d_gbs_per_rank_min": h2d_min,
+                       "path": "run_sharded_stream: detect_stream over the rank's shard in batches of "
+                               f"{B} from pinned host frames, outputs gathered on rank 0 in stream order",
+                       "time": "host wall clock from a barrier to the gathered outputs, max over ranks"}
+        barrier()
+
     # ---- latency of one batch of 1 and of 3 frames (config 5's latency runs), frames on the device ----
     latency = {}
     for nb in (1, 3):
@@ -300,6 +349,7 @@ def run_ours(args, rank: int, world: int):
                     "d2h_bytes_per_step": int(B * 300 * 15 * 4),
                     "path": "FastBasketballDetector.detect_stream(pinned uint8 frame batches) -> numpy, "
                             "H2D / D2H on a copy stream overlapping the neighbouring steps' compute"},
+            "stream": stream_line,
             "gpu_launches": int(launches_per_step * args.steps),
             "roofline": roofline, "kernels": kernels, "clocks": clk.summary(),
             "latency_ms": dict(latency, note="median CUDA-event time of preprocessing + forward for one batch, "
@@ -325,6 +375,8 @@ def main():
                     help="frames per step per GPU (64: config 5's 512-frame stream over 8 GPUs)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--stream-frames", type=int, default=512,
+                    help="frames of the sharded stream measurement (0 skips it)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))

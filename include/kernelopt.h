@@ -46,7 +46,7 @@ typedef struct CUstream_st* ko_stream_t; /* identical to cudaStream_t */
 
 /* Activations of ko_linear_f32_packed. */
 #define KO_ACT_NONE 0
-#define KO_ACT_GELU 1 /* exact erf GELU: 0.5 v (1 + erf(v / sqrt 2)) */
+#define KO_ACT_GELU 1 /* GELU 0.5 v (1 + erf(v / sqrt 2)), erf by A&S 7.1.26 (|error| < 1.5e-7) */
 #define KO_ACT_RELU 2
 #define KO_ACT_SILU 3 /* v / (1 + exp(-v)); ko_layernorm only */
 

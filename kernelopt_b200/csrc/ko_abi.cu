@@ -48,6 +48,14 @@ const DeviceInfo& device_info() {
   return d;
 }
 
+int device_or_fail(const DeviceInfo** info, const char* who) {
+  const DeviceInfo& d = device_info();
+  if (d.sm_count <= 0)
+    return fail(KO_ERR_UNSUPPORTED, std::string(who) + ": no usable CUDA device is current (attribute query failed)");
+  *info = &d;
+  return KO_OK;
+}
+
 EncodeTiledFn encode_tiled() {
   static EncodeTiledFn fn = nullptr;
   static std::once_flag once;

@@ -585,7 +585,10 @@ extern "C" int ko_attention_f32(const float* q, const float* k, const float* v, 
                             BKEY, 32, CU_TENSOR_MAP_SWIZZLE_128B, "ko_attention_f32 k");
   if (rc) return rc;
   dim3 grid(static_cast<unsigned>((L + BQ - 1) / BQ), static_cast<unsigned>(heads), static_cast<unsigned>(batch));
-  const ko::DeviceInfo& info = ko::device_info();
+  const ko::DeviceInfo* dinfo = nullptr;
+  rc = ko::device_or_fail(&dinfo, who);
+  if (rc) return rc;
+  const ko::DeviceInfo& info = *dinfo;
   if (head_dim == 64) {
     using C = AttnCfg<64>;
     if (static_cast<int64_t>(C::kSmemBytes) > info.max_smem_optin)

@@ -25,6 +25,9 @@ struct DeviceInfo {
   int major = 0, minor = 0;
 };
 const DeviceInfo& device_info();
+// device_info() of the current device, or KO_ERR_UNSUPPORTED (with a message naming `who`) when no usable CUDA
+// device is current (its SM count is unknown): every launching entry point calls this before sizing a grid.
+int device_or_fail(const DeviceInfo** info, const char* who);
 
 // cuTensorMapEncodeTiled obtained through the runtime's driver entry point (no link against libcuda).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

@@ -3,7 +3,7 @@
 //   out[M][N] = act(x[M][K] @ W[K][N] + bias[N])
 //
 // Semantics: the reference's fused fc1 kernel fast_rfdetr/kernels.py:188-266 (gemm_bias_gelu_f32, with the
-// exact-erf GELU epilogue) and its unfused form model.py:142-143 (lin + 0.5*y*(1+erf(y/sqrt 2))).
+// erf GELU epilogue; here the erf is Abramowitz & Stegun 7.1.26) and its unfused form model.py:142-143 (lin + 0.5*y*(1+erf(y/sqrt 2))).
 //
 // Precision: 3xTF32 (the error-compensated split of Ootomo & Yokota, 2022, also known as CUTLASS "3xTF32").
 // Every operand is split as v = hi + lo with hi = tf32_rn(v) and lo = tf32_rn(v - hi); the tensor cores
@@ -845,7 +845,10 @@ int launch_gemm(const float* x, const float* w_packed, const float* bias, int64_
   CUtensorMap mout;
   st = ko::make_tmap_2d_f32(&mout, out, M, N, N, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, "ko_linear out");
   if (st) return st;
-  const ko::DeviceInfo& info = ko::device_info();
+  const ko::DeviceInfo* dinfo = nullptr;
+  st = ko::device_or_fail(&dinfo, "ko_linear");
+  if (st) return st;
+  const ko::DeviceInfo& info = *dinfo;
   if (static_cast<int64_t>(C::kSmemBytes) > info.max_smem_optin)
     return ko::fail(KO_ERR_UNSUPPORTED, "ko_linear: not enough shared memory on this device");
   cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, BKB, SPLIT, EPI_ACT>,
@@ -896,7 +899,10 @@ int launch_gemm_ln(const float* x, const float* w_packed, const float* bias, con
   st = ko::make_tmap_2d_f32(&mr, resid ? resid : y, M, N, N, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B,
                             "ko_linear_residual_ln resid");
   if (st) return st;
-  const ko::DeviceInfo& info = ko::device_info();
+  const ko::DeviceInfo* dinfo = nullptr;
+  st = ko::device_or_fail(&dinfo, "ko_linear_residual_ln");
+  if (st) return st;
+  const ko::DeviceInfo& info = *dinfo;
   if (static_cast<int64_t>(C::kSmemBytes) > info.max_smem_optin)
     return ko::fail(KO_ERR_UNSUPPORTED, "ko_linear_residual_ln: not enough shared memory on this device");
   auto kernel = gemm_tf32x3_kernel<BN, BKB, SPLIT, EPI_LN>;
@@ -976,18 +982,20 @@ const Variant kVariants[] = {
     {128, 128, 1, launch_gemm<128, 128, true>}, {128, 128, 0, launch_gemm<128, 128, false>},
 };
 
-// Tuning override for measurements: KO_GEMM_VARIANT="bn,bkb,split" (e.g. "256,64,1").
+// Measurement builds may pin one variant at compile time (-DKO_GEMM_FORCE_VARIANT=bn,bkb,split); the shipped
+// library chooses by shape only.
 const Variant* forced_variant() {
+#ifdef KO_GEMM_FORCE_VARIANT
   static const Variant* v = [] {
-    const char* env = getenv("KO_GEMM_VARIANT");
-    if (!env) return static_cast<const Variant*>(nullptr);
-    int bn = 0, bkb = 0, split = 0;
-    if (sscanf(env, "%d,%d,%d", &bn, &bkb, &split) != 3) return static_cast<const Variant*>(nullptr);
+    const int want[3] = {KO_GEMM_FORCE_VARIANT};
     for (const Variant& c : kVariants)
-      if (c.bn == bn && c.bkb == bkb && c.split == split) return &c;
+      if (c.bn == want[0] && c.bkb == want[1] && c.split == want[2]) return &c;
     return static_cast<const Variant*>(nullptr);
   }();
   return v;
+#else
+  return nullptr;
+#endif
 }
 
 // Default choice.
@@ -1000,10 +1008,9 @@ const Variant* forced_variant() {
 //   model's shapes. 192-wide tiles take A from tensor memory (7-10 % faster than with A in shared memory); wider
 //   tiles read each x tile for more columns; with SPLIT, 256-wide tiles hold all 512 TMEM columns (one buffer)
 //   and lose the overlap of epilogue and MMAs.
-const Variant* choose_variant(int64_t M, int64_t N, int64_t K) {
+const Variant* choose_variant(int64_t M, int64_t N, int64_t K, int64_t sms) {
   if (const Variant* f = forced_variant()) return f;
   const int split = K > 512 ? 1 : 0;
-  const int64_t sms = ko::device_info().sm_count;
   const int64_t m_tiles = (M + BM - 1) / BM;
   const int bns[3] = {256, 192, 128};
   const double cost_plain[3] = {1.0, 1.04, 1.45};
@@ -1054,7 +1061,10 @@ extern "C" int ko_linear_f32_packed(const float* x, const float* w_packed, const
   if (st || M == 0) return st;
   if (act != KO_ACT_NONE && act != KO_ACT_GELU && act != KO_ACT_RELU)
     return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_linear_f32_packed: unknown activation");
-  const Variant* v = choose_variant(M, N, K);
+  const ko::DeviceInfo* info = nullptr;
+  st = ko::device_or_fail(&info, "ko_linear_f32_packed");
+  if (st) return st;
+  const Variant* v = choose_variant(M, N, K, info->sm_count);
   return v->fn(x, w_packed, bias, M, K, N, act, out, dev_status, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -1078,6 +1088,9 @@ extern "C" int ko_linear_residual_ln_f32_packed(const float* x, const float* w_p
     return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": pointers must be 16-byte aligned");
   if (y == resid || y == h_out || y == x)
     return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": y must not alias x, resid or h_out");
+  const ko::DeviceInfo* info = nullptr;
+  st = ko::device_or_fail(&info, who);
+  if (st) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool split = K > 512;
   // N = 256 rows fit one 256-wide CTA or a cluster of two 128-wide ones. With fewer row blocks than two per SM
@@ -1087,7 +1100,7 @@ extern "C" int ko_linear_residual_ln_f32_packed(const float* x, const float* w_p
   const int64_t m_tiles = (M + BM - 1) / BM;
   const int bn = N == 384 ? 192
                  : N == 512 ? 256
-                 : (N == 256 && m_tiles < 2 * static_cast<int64_t>(ko::device_info().sm_count)) ? 128
+                 : (N == 256 && m_tiles < 2 * static_cast<int64_t>(info->sm_count)) ? 128
                                                                                                 : static_cast<int>(N);
 #define KO_LN_CASE(BNV)                                                                                         \
   if (bn == BNV)                                                                                               \
@@ -1142,6 +1155,9 @@ extern "C" int ko_linear_gelu_f32(const float* x, const float* w, const float* b
   if (st || M == 0) return st;
   if (!workspace || !ko::aligned16(workspace) || workspace_bytes < ko_linear_workspace_bytes(K, N))
     return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_linear_gelu_f32: workspace missing, unaligned or too small");
+  const ko::DeviceInfo* info = nullptr;
+  st = ko::device_or_fail(&info, "ko_linear_gelu_f32");
+  if (st) return st;
   float* packed = static_cast<float*>(workspace);
   st = ko_pack_weight_tf32x3(w, K, N, packed, stream);
   if (st) return st;
@@ -1211,6 +1227,9 @@ extern "C" int ko_linear_gelu_f32_noalloc(const float* x, const float* w, const 
                         " exceeds the static scratch of KO_NOALLOC_MAX_WEIGHT_ELEMS = " +
                         std::to_string(static_cast<long long>(KO_NOALLOC_MAX_WEIGHT_ELEMS)) +
                         " weight elements; use ko_linear_gelu_f32 with a workspace instead");
+  const ko::DeviceInfo* info = nullptr;
+  st = ko::device_or_fail(&info, "ko_linear_gelu_f32_noalloc");
+  if (st) return st;
   float* scratch = nullptr;
   st = noalloc_scratch(&scratch);
   if (st) return st;

@@ -45,7 +45,9 @@ extern "C" int ko_im2col3x3(const float* x, int64_t B, int64_t H, int64_t W, int
   if (!x || !cols || !ko::aligned16(x) || !ko::aligned16(cols))
     return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_im2col3x3: pointers must be non-null and 16-byte aligned");
   const int64_t total = B * H * W * 9 * (C / 4);
-  const int64_t sms = ko::device_info().sm_count;
+  const ko::DeviceInfo* info = nullptr;
+  if (int st = ko::device_or_fail(&info, "ko_im2col3x3")) return st;
+  const int64_t sms = info->sm_count;
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, sms * 8);
   im2col3x3_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const float4*>(x), static_cast<int>(B), static_cast<int>(H), static_cast<int>(W),

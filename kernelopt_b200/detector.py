@@ -46,6 +46,8 @@ def load_weights(model_path: str | Path, cache_dir: str | Path | None = None) ->
 
     model_path may be
       * "random:<seed>"           seeded random-init weights (weights.random_weights)
+      * "random-varied:<seed>"    the same with non-identity biases, norms, layer scales and proposal mask
+                                  (weights.random_weights(seed, varied=True))
       * a .safetensors file       e.g. the reference's own cache, mlx-cache/<digest>/weights.safetensors
       * an .onnx file             read through the reference's cache layout: <cache_dir or
                                   model_dir/mlx-cache/<sha256[:20]>>/weights.safetensors must exist (extracting
@@ -53,6 +55,8 @@ def load_weights(model_path: str | Path, cache_dir: str | Path | None = None) ->
     s = str(model_path)
     if s.startswith("random:"):
         return W.random_weights(int(s.split(":", 1)[1] or 0))
+    if s.startswith("random-varied:"):
+        return W.random_weights(int(s.split(":", 1)[1] or 0), varied=True)
     path = Path(model_path)
     if path.suffix == ".safetensors":
         return W.load(path)
@@ -254,13 +258,20 @@ class FastBasketballDetector:
             K.check_device_status(self.device)
             return out_host[s][0].numpy().copy(), out_host[s][1].numpy().copy()
 
-        enqueue(0, first)
-        i = 0
-        for frames in it:
-            enqueue(i + 1, frames)
+        try:
+            enqueue(0, first)
+            i = 0
+            for frames in it:
+                enqueue(i + 1, frames)
+                yield collect(i)
+                i += 1
             yield collect(i)
-            i += 1
-        yield collect(i)
+        finally:
+            # A consumer that stops early (break, an exception) must not free the slot buffers while copies or
+            # preprocessing that use them are still queued: the caching allocator would hand them out again.
+            h2d.synchronize()
+            self.stream.synchronize()
+            d2h.synchronize()
 
     def detect_frames(self, frames: torch.Tensor) -> tuple[np.ndarray, np.ndarray]:
         """Frames already in a uint8 tensor [N, H, W, 3] (one size), ideally in pinned host memory (a video

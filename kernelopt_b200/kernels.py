@@ -414,18 +414,24 @@ def linear_gelu_f32(x, w, bias):
     """GELU(x @ w + bias) for float32 x [..., K], w [K, N], bias [N] (kernels.py:271-285).
 
     The split of w is cached per weight tensor (and redone if the tensor is modified in place). A new split is
-    complete before it enters the cache, so callers on other streams can use it at once (outside graph capture)."""
+    complete before it enters the cache, so callers on other streams can use it at once. During CUDA graph
+    capture a missing split is recorded into the graph for this call only and not cached: it holds data only
+    once the graph replays, so an eager call must not find it."""
     _need(x, "x")
     _need(w, "w")
     _need(bias, "bias")
     with _pack_lock:
         hit = _pack_cache.get(w)
         if hit is None or hit[0] != w._version:
-            hit = (w._version, PackedWeight(w))
-            if not torch.cuda.is_current_stream_capturing():
+            if torch.cuda.is_current_stream_capturing():
+                pw = PackedWeight(w)                  # part of the captured graph; lives as long as this call
+            else:
+                hit = (w._version, PackedWeight(w))
                 torch.cuda.current_stream().synchronize()
-            _pack_cache[w] = hit
-    pw = hit[1]
+                _pack_cache[w] = hit
+                pw = hit[1]
+        else:
+            pw = hit[1]
     m = x.numel() // pw.k
     out = torch.empty((*x.shape[:-1], pw.n), dtype=torch.float32, device=x.device)
     call("ko_linear_f32_packed", x.data_ptr(), pw.packed.data_ptr(), bias.data_ptr(), m, pw.k, pw.n,

@@ -4,10 +4,13 @@
 
 Kernels and workloads (per frame of batch B; the algorithmic traffic or flops counted for the roofline):
   preprocess  B frames, sizes cycling 1920x1080 / 1280x720 / 960x540 (B=1: 1080p only), seeded noise,
-              PATCH16 output; bytes = H*W*3 read + 640*640*3*4 written per frame
+              PATCH16 output; bytes = H*W*3 read + 640*640*3*4 written per frame (--policy picks the tables)
+  preprocess_1080p  the benchmark's frames: B seeded 1920x1080 noise frames, PATCH16 output
   resln       rows = B*1600, C = 384, x/residual ~ N(0,1); bytes = 4 * rows * 384 * 4
   gemm        GELU(A @ W + b), A [B*1600, 384] ~ N(0,1), W [384, 1536] ~ N(0, 0.02^2); flops = 2*M*384*1536
   deform      value [B,1600,16,16], loc U[-0.05,1.05], softmax aw; bytes = 2,060,800 per frame
+  deform_model the decoder's layout: value [B,1600,1024] (four layers' projections side by side), layer 1's
+              columns [256, 512); the same bytes per frame (the layer's slice of the map is what is sampled)
   attn        the backbone's global attention: B frames x 1604 tokens x 6 heads x 64, q/k/v column slices of
               one [B, 1604, 1152] projection ~ N(0,1); flops = 4 * B * 6 * 1604^2 * 64
   attn_win    the windowed attention: 4B windows x 401 tokens x 6 heads x 64; flops = 4 * 4B * 6 * 401^2 * 64
@@ -35,17 +38,17 @@ from .resize_tables import tables
 SIZES = [(1080, 1920), (720, 1280), (540, 960)]
 
 
-def setup(kernel: str, b: int, dev):
+def setup(kernel: str, b: int, dev, policy: str = "reference"):
     g = torch.Generator(device="cpu").manual_seed(0)
-    if kernel == "preprocess":
+    if kernel in ("preprocess", "preprocess_1080p"):
         rng = np.random.default_rng(0)
-        sizes = [SIZES[0]] if b == 1 else [SIZES[i % 3] for i in range(b)]
+        sizes = [SIZES[0]] if b == 1 or kernel == "preprocess_1080p" else [SIZES[i % 3] for i in range(b)]
         lut = (np.arange(256, dtype=np.float32)[:, None] / 255. - np.asarray([.485, .456, .406], np.float32)) \
             / np.asarray([.229, .224, .225], np.float32)
         lut_d = torch.from_numpy(np.ascontiguousarray(lut.T)).to(dev)
         items = []
         for h, w in sizes:
-            mode, xt, yt = tables(w, h)
+            mode, xt, yt = tables(w, h, policy=policy)
             img = torch.from_numpy(rng.integers(0, 256, (h, w, 3), dtype=np.uint8)).to(dev)
             items.append((img, torch.from_numpy(np.array(xt)).to(dev), torch.from_numpy(np.array(yt)).to(dev), mode))
         out = torch.empty((b, 1600, 768), device=dev)
@@ -93,6 +96,11 @@ def setup(kernel: str, b: int, dev):
         loc = (torch.rand(b, 300, 16, 2, 2, generator=g) * 1.1 - 0.05).to(dev)
         aw = torch.softmax(torch.randn(b, 300, 16, 2, generator=g), -1).to(dev)
         return (lambda: K.deform_attn(value, loc, aw, (40, 40), 16, 16)), 2060800.0 * b, "byte"
+    if kernel == "deform_model":
+        value = torch.randn(b, 1600, 1024, generator=g).to(dev)
+        loc = (torch.rand(b, 300, 16, 2, 2, generator=g) * 1.1 - 0.05).to(dev)
+        aw = torch.softmax(torch.randn(b, 300, 16, 2, generator=g), -1).to(dev)
+        return (lambda: K.deform_attn(value, loc, aw, (40, 40), 16, 16, offset=256)), 2060800.0 * b, "byte"
     if kernel in ("attn", "attn_win"):
         nb, n = (b, 1604) if kernel == "attn" else (4 * b, 401)
         qkv = torch.randn(nb, n, 1152, generator=g).to(dev)
@@ -103,15 +111,18 @@ def setup(kernel: str, b: int, dev):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", required=True, choices=["preprocess", "resln", "gemm", "deform", "attn", "attn_win",
+    ap.add_argument("--kernel", required=True, choices=["preprocess", "preprocess_1080p", "resln", "gemm", "deform", "deform_model",
+                                                             "attn", "attn_win",
                                                              "outproj_ln", "outproj_unfused", "fc2_ln", "fc2_unfused", "qkv"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--policy", choices=["reference", "opencv"], default="reference",
+                    help="resize tables of the preprocess kernels")
     args = ap.parse_args()
     torch.backends.cuda.matmul.allow_tf32 = False
     dev = torch.device("cuda:0")
-    fn, work, unit = setup(args.kernel, args.batch, dev)
+    fn, work, unit = setup(args.kernel, args.batch, dev, args.policy)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)   # 256 MB > L2
     for _ in range(args.warmup):
         fn()

@@ -2,10 +2,12 @@
 runs whole frames through its own detector, and only the small outputs (300 x 15 floats per frame) travel back.
 
 Two runners:
-  * shard_range / run_sharded: one process per GPU (torch.distributed, launched by torchrun). Rank r takes a
-    contiguous shard of the stream, produces its frames itself (decoder or generator, frame index -> image),
-    and rank 0 gathers the outputs in stream order (an object gather of host arrays; the process group may be
-    nccl or gloo).
+  * shard_range / run_sharded / run_sharded_stream: one process per GPU (torch.distributed, launched by
+    torchrun). Rank r takes a contiguous shard of the stream, produces its frames itself (decoder or generator,
+    frame index -> image), and rank 0 gathers the outputs in stream order (an object gather of host arrays; the
+    process group may be nccl or gloo). run_sharded calls a batch detector per batch; run_sharded_stream feeds
+    the shard as uint8 frame batches to a pipelined detector (FastBasketballDetector.detect_stream), so copies
+    in and out overlap the compute of the neighbouring batches.
   * QueueRunner: one process driving several GPUs from worker threads that pull batches from a shared queue.
     If a worker fails (an exception from its detector: a launch error, a device-side timeout reported by
     check_device_status, a lost device), its batch goes back on the queue for the surviving workers and the
@@ -43,7 +45,31 @@ def run_sharded(detect: DetectFn, frame_at: Callable[[int], np.ndarray], n_frame
         b, lg = detect([frame_at(i) for i in range(s, min(s + batch, idx.stop))])
         boxes.append(b)
         logits.append(lg)
-    mine = (idx.start, np.concatenate(boxes) if boxes else np.zeros((0, 300, 4), np.float32),
+    return _gather(idx.start, boxes, logits, rank, world, group)
+
+
+def run_sharded_stream(detect_stream: Callable, batch_at: Callable, n_frames: int, batch: int, group=None):
+    """run_sharded for a pipelined detector. detect_stream(iterable of frame batches) yields (boxes, logits) per
+    batch in order; batch_at(start, stop) returns the frames [start, stop) of the stream as one batch (e.g. a
+    uint8 tensor [stop - start, H, W, 3] in pinned host memory). Full batches go through one detect_stream
+    pass and a shorter last batch through a second one (a pipelined stream keeps one batch shape). Gathers
+    (boxes [n,300,4], logits [n,300,11]) on rank 0 in stream order; other ranks return None."""
+    import torch.distributed as dist
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    idx = shard_range(n_frames, rank, world)
+    full = [(s, s + batch) for s in range(idx.start, idx.stop - batch + 1, batch)]
+    tail = [(full[-1][1] if full else idx.start, idx.stop)]
+    boxes, logits = [], []
+    for spans in (full, [t for t in tail if t[1] > t[0]]):
+        for b, lg in detect_stream(batch_at(s, e) for s, e in spans):
+            boxes.append(b)
+            logits.append(lg)
+    return _gather(idx.start, boxes, logits, rank, world, group)
+
+
+def _gather(start: int, boxes: list, logits: list, rank: int, world: int, group):
+    import torch.distributed as dist
+    mine = (start, np.concatenate(boxes) if boxes else np.zeros((0, 300, 4), np.float32),
             np.concatenate(logits) if logits else np.zeros((0, 300, 11), np.float32))
     parts = [None] * world if rank == 0 else None
     dist.gather_object(mine, parts, dst=0, group=group)

@@ -9,6 +9,11 @@ provides what the rest of the path needs:
     Init: truncated normal (std 0.02, cut at 2 std) for every weight matrix, conv kernel and embedding;
     biases 0; LayerNorm gamma 1, beta 0; layer-scale lambdas 1.0; decoder FFN width 2048 (the RF-DETR default,
     not pinned by the reference). LayerNorm eps: 1e-6 in the backbone and projector, 1e-5 in the transformer.
+    `random_weights(seed, varied=True)` exercises every parameter the init above leaves at an identity value:
+    biases ~ 0.02 * tn, LayerNorm gamma ~ 1 + 0.1 * tn and beta ~ 0.05 * tn, layer-scale lambdas ~ 1 + 0.2 * tn
+    (tn: standard normal cut at 2), and a proposal mask with the four corner proposals marked invalid (the
+    reference's proposals are all valid, fast_rfdetr/weights.py:81-88; the model still multiplies by the mask,
+    model.py:177).
   * `proposals()`  the fixed 40x40 encoder proposals and validity mask (fast_rfdetr/weights.py:81-88).
   * `save` / `load`  safetensors files with the same schema — including the reference's own weight cache
     (mlx-cache/<digest>/weights.safetensors), which therefore loads here unchanged.
@@ -42,39 +47,53 @@ def dim_t(n: int = 128, temperature: float = 10000.0) -> np.ndarray:
     return (temperature ** (2 * (i // 2) / n)).astype(np.float32)
 
 
-def random_weights(seed: int = 0) -> dict[str, np.ndarray]:
+def random_weights(seed: int = 0, varied: bool = False) -> dict[str, np.ndarray]:
     rng = np.random.default_rng(seed)
+    # the varied parameters come from a second stream, so the weight matrices equal those of varied=False
+    vrng = np.random.default_rng([seed, 1]) if varied else None
     w: dict[str, np.ndarray] = {}
 
-    def tn(*shape):
-        return np.clip(rng.standard_normal(shape), -2.0, 2.0).astype(np.float32) * np.float32(0.02)
+    def tn(*shape, std=0.02):
+        return np.clip(rng.standard_normal(shape), -2.0, 2.0).astype(np.float32) * np.float32(std)
 
-    def lin(key, n_in, n_out, bias=True):
+    def around(n, centre, std):
+        if vrng is None:
+            return np.full(n, centre, np.float32)
+        return (np.float32(centre) + np.clip(vrng.standard_normal(n), -2.0, 2.0).astype(np.float32)
+                * np.float32(std)).astype(np.float32)
+
+    def bias(n):
+        return around(n, 0.0, 0.02)
+
+    def scale(n):
+        return around(n, 1.0, 0.2)
+
+    def lin(key, n_in, n_out, with_bias=True):
         w[key + ".weight"] = tn(n_in, n_out)
-        if bias:
-            w[key + ".bias"] = np.zeros(n_out, np.float32)
+        if with_bias:
+            w[key + ".bias"] = bias(n_out)
 
     def ln(key, n, eps):
-        w[key + ".weight"] = np.ones(n, np.float32)
-        w[key + ".bias"] = np.zeros(n, np.float32)
+        w[key + ".weight"] = around(n, 1.0, 0.1)
+        w[key + ".bias"] = around(n, 0.0, 0.05)
         w["_eps." + key + ".weight"] = np.asarray(eps, np.float32)
 
     # backbone (DINOv2-small style windowed ViT)
     w[BB + "embeddings.cls_token"] = tn(1, 1, C)
     w[BB + "embeddings.position_embeddings"] = tn(1, 1601, C)
     w[BB + "embeddings.patch_embeddings.projection.weight"] = tn(C, 16, 16, 3)
-    w[BB + "embeddings.patch_embeddings.projection.bias"] = np.zeros(C, np.float32)
+    w[BB + "embeddings.patch_embeddings.projection.bias"] = bias(C)
     for i in range(12):
         pre = LAYER.format(i)
         ln(pre + "norm1", C, 1e-6)
         for n in ("query", "key", "value"):
             lin(pre + "attention.attention." + n, C, C)
         lin(pre + "attention.output.dense", C, C)
-        w[pre + "layer_scale1.lambda1"] = np.ones(C, np.float32)
+        w[pre + "layer_scale1.lambda1"] = scale(C)
         ln(pre + "norm2", C, 1e-6)
         lin(pre + "mlp.fc1", C, MLP)
         lin(pre + "mlp.fc2", MLP, C)
-        w[pre + "layer_scale2.lambda1"] = np.ones(C, np.float32)
+        w[pre + "layer_scale2.lambda1"] = scale(C)
     ln(BB + "layernorm", C, 1e-6)
 
     # projector: C2f with 3 bottlenecks, channel LayerNorm + SiLU after every conv
@@ -91,6 +110,9 @@ def random_weights(seed: int = 0) -> dict[str, np.ndarray]:
 
     # two-stage query selection
     w.update(proposals())
+    if varied:
+        w["proposal_valid"] = w["proposal_valid"].copy()
+        w["proposal_valid"][[0, 39, 1560, 1599]] = 0.0
     lin("transformer.enc_output.0", D_MODEL, D_MODEL)
     ln("transformer.enc_output_norm.0", D_MODEL, 1e-5)
     lin("transformer.enc_out_class_embed.0", D_MODEL, N_CLASSES)
@@ -108,7 +130,7 @@ def random_weights(seed: int = 0) -> dict[str, np.ndarray]:
         for n in ("q", "k", "v"):
             lin(pre + "self_attn." + n, D_MODEL, D_MODEL)
         w[pre + "self_attn.out_proj.weight"] = tn(D_MODEL, D_MODEL)  # stored [out, in] (ONNX Gemm transB=1)
-        w[pre + "self_attn.out_proj.bias"] = np.zeros(D_MODEL, np.float32)
+        w[pre + "self_attn.out_proj.bias"] = bias(D_MODEL)
         ln(pre + "norm1", D_MODEL, 1e-5)
         lin(pre + "cross_attn.sampling_offsets", D_MODEL, CA_HEADS * CA_POINTS * 2)
         lin(pre + "cross_attn.attention_weights", D_MODEL, CA_HEADS * CA_POINTS)

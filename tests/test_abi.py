@@ -89,6 +89,29 @@ def test_linear_workspace_size():
     assert _lib.lib().ko_linear_workspace_bytes(384, 1536) == 2 * 384 * 1536 * 4
 
 
+@pytest.mark.parametrize("call", [
+    ("ko_linear_f32_packed", (16, 16, None, 256, 384, 1536, 0, 16, None, None)),
+    ("ko_linear_gelu_f32", (16, 16, 16, 256, 384, 1536, 16, 16, 2 * 384 * 1536 * 4, None, None)),
+    ("ko_linear_residual_ln_f32_packed",
+     (16, 16, None, None, None, 16, 16, 1e-6, 512, 384, 256, 0, None, 32, None, None)),
+    ("ko_conv3x3_ln_f32_packed", (16, 16, 16, 16, 16, 1e-6, 1, 8, 8, 16, 256, 0, 32, None, None)),
+    ("ko_attention_f32", (16, 16, 16, 32, 1, 128, 1, 64, 0, 64, 0, 64, 0, 64, 0, 64, 0.125, None, None)),
+    ("ko_im2col3x3", (16, 1, 8, 8, 8, 32, None)),
+])
+def test_valid_calls_without_a_device_fail_cleanly(call):
+    """With no usable CUDA device the SM count is unknown: a well-formed call must return KO_ERR_UNSUPPORTED with
+    a message before it sizes a grid (no division by a zero SM count, no zero-block launch)."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    name, args = call
+    with pytest.raises(_lib.KernelError) as e:
+        _lib.call(name, *args)
+    assert e.value.status == _lib.KO_ERR_UNSUPPORTED
+    assert _lib.lib().ko_last_error_string()
+
+
 def test_check_device_reports_a_missing_gpu():
     """Without a CUDA device the device check fails cleanly (KO_ERR_UNSUPPORTED and a message) on every call."""
     import torch

@@ -394,6 +394,33 @@ def test_linear_gelu_special_values(cuda):
     assert torch.equal(y[5:], torch.zeros(123, 16))
 
 
+def test_linear_gelu_split_made_during_capture_is_not_cached(cuda):
+    """A weight first seen inside CUDA graph capture: its split exists only once the graph replays, so an eager
+    call before the replay must split it again rather than read the graph's unfilled buffer."""
+    r = np.random.default_rng(33)
+    x = r.standard_normal((512, 384)).astype(np.float32)
+    w = (0.02 * r.standard_normal((384, 768))).astype(np.float32)
+    b = (0.01 * r.standard_normal(768)).astype(np.float32)
+    ref = OK.linear_gelu_f32(x, w, b)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    xd, wd, bd = t(x), t(w), t(b)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            captured = K.linear_gelu_f32(xd, wd, bd)
+    eager = K.linear_gelu_f32(xd, wd, bd)            # before any replay
+    torch.cuda.synchronize()
+    assert_close(eager, ref, what="eager after capture")
+    g.replay()
+    torch.cuda.synchronize()
+    K.check_device_status()
+    assert_close(captured, ref, what="replayed graph")
+    assert torch.equal(captured, eager)
+    del g
+
+
 @pytest.mark.parametrize("act", [None, "relu"])
 def test_linear_packed_acts(cuda, act):
     r = np.random.default_rng(9)

@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch.multiprocessing as mp
 
-from kernelopt_b200.stream import QueueRunner, WorkerFailed, run_sharded, shard_range
+from kernelopt_b200.stream import QueueRunner, WorkerFailed, run_sharded, run_sharded_stream, shard_range
 
 
 def fake_frame(i: int) -> np.ndarray:
@@ -31,11 +31,24 @@ def test_shard_range_covers_stream():
         assert max(len(s) for s in shards) - min(len(s) for s in shards) <= 1
 
 
-def _rank_main(rank, world, port, n, out_path):
+def fake_detect_stream(batches):
+    """A pipelined detector's contract: one (boxes, logits) per batch, in order, every batch of one shape."""
+    shape = None
+    for frames in batches:
+        shape = shape or frames.shape
+        assert frames.shape == shape, "a pipelined stream keeps one batch shape"
+        yield fake_detect(list(frames))
+
+
+def _rank_main(rank, world, port, n, out_path, pipelined=False):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    res = run_sharded(fake_detect, fake_frame, n, batch=5)
+    if pipelined:
+        res = run_sharded_stream(fake_detect_stream, lambda s, e: np.stack([fake_frame(i) for i in range(s, e)]),
+                                 n, batch=5)
+    else:
+        res = run_sharded(fake_detect, fake_frame, n, batch=5)
     if rank == 0:
         np.save(out_path, res[0][:, 0, 0])
     else:
@@ -50,6 +63,18 @@ def test_run_sharded_two_gloo_ranks(tmp_path):
     out = tmp_path / "ids.npy"
     mp.start_processes(_rank_main, args=(2, port, 23, str(out)), nprocs=2, join=True, start_method="spawn")
     assert np.array_equal(np.load(out), np.arange(23, dtype=np.float32))
+
+
+@pytest.mark.parametrize("n", [23, 20, 3])
+def test_run_sharded_stream_two_gloo_ranks(tmp_path, n):
+    """Shards of 12 + 11 frames in batches of 5 (full batches, then a shorter tail through a second pass), shards
+    that are whole batches, and shards shorter than one batch: outputs come back on rank 0 in stream order."""
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    out = tmp_path / "ids.npy"
+    mp.start_processes(_rank_main, args=(2, port, n, str(out), True), nprocs=2, join=True, start_method="spawn")
+    assert np.array_equal(np.load(out), np.arange(n, dtype=np.float32))
 
 
 def test_queue_runner_requeues_failed_batch():

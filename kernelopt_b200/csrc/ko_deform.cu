@@ -130,75 +130,6 @@ __global__ void __launch_bounds__(256) deform_vec4_np2_kernel(const float* __res
   reinterpret_cast<float4*>(out)[t] = acc;
 }
 
-// Two points per head and an even head count (the model: 16 heads): each thread serves two (query, head) items,
-// heads h and h + NH/2 of one query, and issues all 16 of their tap loads before the first multiply — twice the
-// independent 16-byte gathers in flight per thread of deform_vec4_np2_kernel, for a gather whose time is load
-// latency. A warp still covers 8 heads x 4 channel groups per item, so each of its two stores is one contiguous
-// 512-byte run of the output row.
-__global__ void __launch_bounds__(256) deform_vec4_np2_x2_kernel(const float* __restrict__ value,
-                                                                 const float* __restrict__ loc,
-                                                                 const float* __restrict__ aw, DeformShape s,
-                                                                 float* __restrict__ out) {
-  const int64_t groups = s.HD >> 2;
-  const int64_t half = s.NH >> 1;
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t total = s.B * s.NQ * half * groups;
-  if (t >= total) return;
-  const int64_t g = t % groups;
-  const int64_t hh = (t / groups) % half;
-  const int64_t bq = t / (groups * half);  // b*NQ + q
-  const int64_t b = bq / s.NQ;
-  const int GW = static_cast<int>(s.GW), GH = static_cast<int>(s.GH);
-  const float* vrow = value + b * (s.GH * s.GW * s.ROW) + s.offset + g * 4;
-  int64_t qh[2];
-  float4 l[2];
-  float2 w[2];
-#pragma unroll
-  for (int it = 0; it < 2; ++it) {
-    qh[it] = bq * s.NH + hh + it * half;
-    l[it] = __ldg(reinterpret_cast<const float4*>(loc) + qh[it]);   // (x0, y0, x1, y1)
-    w[it] = __ldg(reinterpret_cast<const float2*>(aw) + qh[it]);
-  }
-  float4 v[16];
-  float wt[16];
-#pragma unroll
-  for (int it = 0; it < 2; ++it) {
-    const float* vb = vrow + (hh + it * half) * s.HD;
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      const float lx = (p ? l[it].z : l[it].x) * static_cast<float>(GW) - 0.5f;
-      const float ly = (p ? l[it].w : l[it].y) * static_cast<float>(GH) - 0.5f;
-      const float x0f = floorf(lx), y0f = floorf(ly);
-      const float fx = lx - x0f, fy = ly - y0f;
-      const int x0 = static_cast<int>(x0f), y0 = static_cast<int>(y0f);
-#pragma unroll
-      for (int dy = 0; dy < 2; ++dy) {
-#pragma unroll
-        for (int dx = 0; dx < 2; ++dx) {
-          const int k = it * 8 + p * 4 + dy * 2 + dx;
-          const int yy = y0 + dy, xx = x0 + dx;
-          const bool in = yy >= 0 && yy < GH && xx >= 0 && xx < GW;
-          wt[k] = in ? (dx ? fx : 1.0f - fx) * (dy ? fy : 1.0f - fy) : 0.0f;
-          v[k] = in ? __ldg(reinterpret_cast<const float4*>(vb + static_cast<int64_t>(yy * GW + xx) * s.ROW))
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int it = 0; it < 2; ++it) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      float4 sacc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) fma4(sacc, wt[it * 8 + p * 4 + k], v[it * 8 + p * 4 + k]);
-      fma4(acc, p ? w[it].y : w[it].x, sacc);
-    }
-    reinterpret_cast<float4*>(out)[qh[it] * groups + g] = acc;
-  }
-}
-
 // General layout: one thread per (b, q, h, d).
 __global__ void __launch_bounds__(256) deform_scalar_kernel(const float* __restrict__ value,
                                                             const float* __restrict__ loc,
@@ -258,10 +189,7 @@ extern "C" int ko_deform_attn(const float* value, const float* loc, const float*
   if (blocks > 0x7fffffff) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_deform_attn: problem too large");
   const bool np2 = vec && NP == 2 && (reinterpret_cast<uintptr_t>(loc) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(aw) & 7) == 0;
-  if (np2 && NH % 2 == 0)
-    deform_vec4_np2_x2_kernel<<<static_cast<unsigned>((total / 2 + 255) / 256), 256, 0, st>>>(value, loc, aw, s,
-                                                                                               out);
-  else if (np2)
+  if (np2)
     deform_vec4_np2_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(value, loc, aw, s, out);
   else if (vec)
     deform_vec4_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(value, loc, aw, s, out);

@@ -164,6 +164,9 @@ __device__ __forceinline__ float gelu_as7126(float v) {
 }
 
 __device__ __forceinline__ float apply_act(float v, int act) {
+#ifdef KO_GELU_ERFF  // measurement builds: CUDA's erff instead of A&S 7.1.26, to size the formula's share of error
+  if (act == KO_ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f));
+#endif
   if (act == KO_ACT_GELU) return gelu_as7126(v);
   if (act == KO_ACT_RELU) return fmaxf(v, 0.0f);
   return v;
@@ -1008,9 +1011,12 @@ const Variant* forced_variant() {
 //   model's shapes. 192-wide tiles take A from tensor memory (7-10 % faster than with A in shared memory); wider
 //   tiles read each x tile for more columns; with SPLIT, 256-wide tiles hold all 512 TMEM columns (one buffer)
 //   and lose the overlap of epilogue and MMAs.
+#ifndef KO_SPLIT_MIN_K
+#define KO_SPLIT_MIN_K 512  // measurement builds may move the threshold (-DKO_SPLIT_MIN_K=0: SPLIT everywhere)
+#endif
 const Variant* choose_variant(int64_t M, int64_t N, int64_t K, int64_t sms) {
   if (const Variant* f = forced_variant()) return f;
-  const int split = K > 512 ? 1 : 0;
+  const int split = K > KO_SPLIT_MIN_K ? 1 : 0;
   const int64_t m_tiles = (M + BM - 1) / BM;
   const int bns[3] = {256, 192, 128};
   const double cost_plain[3] = {1.0, 1.04, 1.45};
@@ -1092,7 +1098,7 @@ extern "C" int ko_linear_residual_ln_f32_packed(const float* x, const float* w_p
   st = ko::device_or_fail(&info, who);
   if (st) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const bool split = K > 512;
+  const bool split = K > KO_SPLIT_MIN_K;
   // N = 256 rows fit one 256-wide CTA or a cluster of two 128-wide ones. With fewer row blocks than two per SM
   // (the decoder's 300 queries per frame), the pair halves each row block's time and wins (fc2, K = 2048: 225 ->
   // 196 us at 64 frames); with many row blocks the single CTA keeps its wider tile (158 against 185 us at 102400
@@ -1132,7 +1138,7 @@ extern "C" int ko_conv3x3_ln_f32_packed(const float* x, const float* w_packed, c
     return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": gamma, beta required and 16-byte aligned; eps >= 0");
   if (y == x) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": y must not alias x");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const bool split = K > 512;
+  const bool split = K > KO_SPLIT_MIN_K;
   const int bn = N == 384 ? 192 : N == 512 ? 256 : static_cast<int>(N);
   const int h = static_cast<int>(H), w = static_cast<int>(W), c = static_cast<int>(C);
 #define KO_CONV_CASE(BNV)                                                                                        \

@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(const __grid_const
 // ---------------------------------------------------------------------------------------------------------
 // Threads per band CTA (measurement builds may override it: -DKO_PRE_BAND_THREADS=n, a multiple of 32 <= 1024).
 #ifndef KO_PRE_BAND_THREADS
-#define KO_PRE_BAND_THREADS 512
+#define KO_PRE_BAND_THREADS 256
 #endif
 constexpr int kBandThreads = KO_PRE_BAND_THREADS;
 // Copies of the normalisation LUT in shared memory: lane i reads copy i % kLutCopies, so a warp's 32 lookups of
@@ -142,7 +142,7 @@ constexpr int kBandThreads = KO_PRE_BAND_THREADS;
 // every lane has a bank of its own, one wavefront per lookup; one copy: ~3.5 wavefronts for random values).
 // Measurement builds may override it (-DKO_PRE_LUT_COPIES=n, a power of two <= 32).
 #ifndef KO_PRE_LUT_COPIES
-#define KO_PRE_LUT_COPIES 32
+#define KO_PRE_LUT_COPIES 1
 #endif
 constexpr int kLutCopies = KO_PRE_LUT_COPIES;
 static_assert(kLutCopies >= 1 && kLutCopies <= 32 && (kLutCopies & (kLutCopies - 1)) == 0, "LUT copies");

@@ -42,7 +42,7 @@ def setup(kernel: str, b: int, dev, policy: str = "reference"):
     g = torch.Generator(device="cpu").manual_seed(0)
     if kernel in ("preprocess", "preprocess_1080p"):
         rng = np.random.default_rng(0)
-        sizes = [SIZES[0]] if b == 1 or kernel == "preprocess_1080p" else [SIZES[i % 3] for i in range(b)]
+        sizes = [SIZES[0]] * b if b == 1 or kernel == "preprocess_1080p" else [SIZES[i % 3] for i in range(b)]
         lut = (np.arange(256, dtype=np.float32)[:, None] / 255. - np.asarray([.485, .456, .406], np.float32)) \
             / np.asarray([.229, .224, .225], np.float32)
         lut_d = torch.from_numpy(np.ascontiguousarray(lut.T)).to(dev)

@@ -213,21 +213,39 @@ def test_batch_matches_single(det):
 
 
 def test_bench_batch_graph_matches_batch_one(det):
-    """The 64-frame captured graph the benchmark times gives, frame for frame, what batch-1 runs give (the bench's
-    own frames: seeded 1080p noise). Different batch sizes may pick different GEMM tiles and LayerNorm CTA
-    layouts, so the bar is the reference's batch-vs-single one; the selections are reported."""
+    """The 64-frame captured graph the benchmark times, against batch-1 runs of the same frames (the bench's own
+    seeded 1080p noise frames). The graph replays exactly the eager 64-frame forward (bitwise). Batch size may
+    change GEMM tiles and LayerNorm CTA layouts, so scores may move in the last bits; where a frame's top-301
+    gaps exceed twice that movement the slot order is provably the same, and there the outputs must agree
+    within the end-to-end bars. Elsewhere the top-300 sets must agree up to near-ties at rank 300."""
+    model = det.model
     frames = np.random.default_rng(1000).integers(0, 256, (64, 1080, 1920, 3), dtype=np.uint8)
-    host = torch.from_numpy(frames).pin_memory()
-    bb, bl = det.detect_frames(host)
-    same_sel, worst_b, worst_l = 0, 0.0, 0.0
-    for k in range(64):
-        sb, sl = det.raw(frames[k])
-        worst_b = max(worst_b, float(np.abs(bb[k] - sb[0]).max()))
-        worst_l = max(worst_l, float(np.abs(bl[k] - sl[0]).max()))
-        same_sel += int(np.array_equal(bb[k], sb[0]))
-    print(f"\n[64-frame graph vs batch 1] max box diff {worst_b:.2e}, max logit diff {worst_l:.2e}, "
-          f"bitwise-equal boxes in {same_sel}/64 frames")
-    assert worst_b < 1e-3 and worst_l < 1e-2
+    gb, gl = det.detect_frames(torch.from_numpy(frames).pin_memory())      # the 64-frame graph
+    x64 = det._runner(64).x.clone()                                         # its preprocessed input
+    with torch.cuda.device(det.device), torch.cuda.stream(det.stream), torch.no_grad():
+        eb, el = model(x64)
+        assert np.array_equal(eb.cpu().numpy(), gb) and np.array_equal(el.cpu().numpy(), gl), \
+            "graph replay differs from the eager forward"
+        s64, i64 = gpu_scores(model, x64)
+        stable = 0
+        for k in range(64):
+            s1, i1 = gpu_scores(model, x64[k:k + 1])
+            move = float(np.abs(s64[k] - s1[0]).max())
+            assert move <= 2e-5, f"frame {k}: batch size moved scores by {move:.2e}"
+            gaps = top_gaps(s1[0], np.ones(1600))
+            if gaps.min() > 2 * move:
+                stable += 1
+                assert np.array_equal(i64[k], i1[0]), f"frame {k}: order differs on a stable ranking"
+                b1, l1 = model(x64[k:k + 1])
+                assert float((b1[0].cpu() - torch.from_numpy(gb[k])).abs().max()) <= BOX_TOL
+                assert float((l1[0].cpu() - torch.from_numpy(gl[k])).abs().max()) <= LOGIT_TOL
+            else:
+                d = set(i64[k].tolist()) ^ set(i1[0].tolist())
+                top = np.sort(s1[0])[::-1]
+                assert all(abs(s1[0][j] - top[299]) <= 4 * move for j in d), f"frame {k}: top-300 sets differ"
+    torch.cuda.synchronize()
+    print(f"\n[64-frame graph vs batch 1] {stable}/64 frames with a provably stable ranking matched within the bars")
+    assert stable >= 8
 
 
 def test_two_instances_two_threads(det):

@@ -180,19 +180,31 @@ int ko_pack_weight_tf32x3(const float* w, int64_t K, int64_t N, float* w_packed,
 int ko_linear_f32_packed(const float* x, const float* w_packed, const float* bias, int64_t M, int64_t K, int64_t N,
                          int act, float* out, int* dev_status, ko_stream_t stream);
 
+/* out = act(x @ W + bias + A) where A[i][j] = addend[i * ld_addend + j] for j < add_cols and 0 beyond: the GEMM
+ * of ko_linear_f32_packed with a per-element term added in its epilogue. add_cols and ld_addend multiples of 4,
+ * 4 <= add_cols <= N, ld_addend >= add_cols, addend 16-byte aligned and not aliasing
+ * out. The decoder uses it for (tgt + qpos) @ W = tgt @ W + qpos @ W, with qpos @ W of all four layers computed
+ * once: it replaces the `tgt + qpos` additions before the self-attention q / k projections and the
+ * cross-attention offset / weight projections (fast_rfdetr/model.py:251, :256) and lets the value projection
+ * of tgt share the q / k GEMM. */
+int ko_linear_add_f32_packed(const float* x, const float* w_packed, const float* bias, const float* addend,
+                             int64_t ld_addend, int64_t add_cols, int64_t M, int64_t K, int64_t N, int act,
+                             float* out, int* dev_status, ko_stream_t stream);
+
 /* GEMM with the residual add and LayerNorm in its epilogue, whole rows at a time:
  *   v = resid + (x @ W + bias) * scale;   y = act((v - mean(v)) / sqrt(var(v) + eps) * gamma + beta)
  * with the mean and biased variance over the N columns of each row. x float32 [M][K]; W pre-split by
  * ko_pack_weight_tf32x3; bias, scale, gamma, beta float32 [N] (bias NULL = 0, scale NULL = 1); resid float32
  * [M][N] or NULL (no residual); h_out float32 [M][N] receives v, or NULL (not written); h_out may alias resid,
- * y must alias none of x, resid, h_out. act KO_ACT_NONE or KO_ACT_SILU. N one of 128, 192, 256, 384, 512 (a
+ * y must alias none of x, resid, h_out; row r of y starts at y + r * ldy (ldy 0 = N; else a multiple of 4 >= N,
+ * so y may be a column slice of a wider buffer). act KO_ACT_NONE or KO_ACT_SILU. N one of 128, 192, 256, 384, 512 (a
  * row spans one CTA, or a cluster of two that exchange row statistics); K % 4 == 0; 16-byte aligned pointers.
  * The GEMM is the 3xTF32 product of ko_linear_f32_packed. Fuses the reference's next step: its attention
  * out-projection and fc2 GEMMs followed by residual_layernorm (fast_rfdetr/model.py:121-123, 129-132,
  * kernels.py:9-67), and also GEMM + LayerNorm + SiLU (model.py:148-158) and GEMM + LayerNorm (model.py:178). */
 int ko_linear_residual_ln_f32_packed(const float* x, const float* w_packed, const float* bias, const float* scale,
                                      const float* resid, const float* gamma, const float* beta, float eps,
-                                     int64_t M, int64_t K, int64_t N, int act, float* h_out, float* y,
+                                     int64_t M, int64_t K, int64_t N, int act, float* h_out, float* y, int64_t ldy,
                                      int* dev_status, ko_stream_t stream);
 
 /* out = GELU_erf(x @ w + bias): packs w into `workspace` (ko_linear_workspace_bytes(K, N) bytes, 16-byte
@@ -218,14 +230,17 @@ int ko_linear_gelu_f32_noalloc(const float* x, const float* w, const float* bias
 /* A 3x3 convolution (stride 1, zero padding 1) as an implicit GEMM on the same tensor cores, with the LayerNorm
  * (+ SiLU) of ko_linear_residual_ln_f32_packed in its epilogue and no residual:
  *   y[p] = act(LN(sum_{ky,kx,c} x[b][py+ky-1][px+kx-1][c] * w[(ky*3+kx)*C + c][:] + bias) * gamma + beta)
- * x: float32 NHWC [B][H][W][C], C % 16 == 0; w_packed: ko_pack_weight_tf32x3 of the weight as [9*C][N] in
- * (ky, kx, c) row order (the conv weight [N][3][3][C] flattened and transposed); y: float32 [B*H*W][N]; N one of
- * 128, 192, 256, 384, 512. No im2col buffer: each k-block's TMA load reads x shifted by the tap, and rows whose
- * shifted pixel lies outside the image are zeroed on chip. Replaces the projector's conv -> channel LayerNorm ->
- * SiLU blocks (fast_rfdetr/model.py:148-158) with one kernel each. */
-int ko_conv3x3_ln_f32_packed(const float* x, const float* w_packed, const float* bias, const float* gamma,
-                             const float* beta, float eps, int64_t B, int64_t H, int64_t W, int64_t C, int64_t N,
-                             int act, float* y, int* dev_status, ko_stream_t stream);
+ * x: float32 NHWC [B][H][W][C] with pixel p at x + p * ldx, C % 16 == 0; w_packed: ko_pack_weight_tf32x3 of the
+ * weight as [9*C][N] in (ky, kx, c) row order (the conv weight [N][3][3][C] flattened and transposed); y: float32
+ * [B*H*W][N] with row p at y + p * ldy; N one of 128, 192, 256, 384, 512; ldx / ldy 0 (= C / N) or multiples of 4
+ * not below C / N, so that x and y can be channel slices of wider NHWC buffers (the projector's concatenation,
+ * fast_rfdetr/model.py:161, is written in place). No im2col buffer: each k-block's TMA load reads x shifted by
+ * the tap, and rows whose shifted pixel lies outside the image are zeroed on chip. Replaces the projector's conv
+ * -> channel LayerNorm -> SiLU blocks (fast_rfdetr/model.py:148-158) with one kernel each. */
+int ko_conv3x3_ln_f32_packed(const float* x, int64_t ldx, const float* w_packed, const float* bias,
+                             const float* gamma, const float* beta, float eps, int64_t B, int64_t H, int64_t W,
+                             int64_t C, int64_t N, int act, float* y, int64_t ldy, int* dev_status,
+                             ko_stream_t stream);
 
 /* --- query selection ------------------------------------------------------------------------------------------ */
 
@@ -253,6 +268,27 @@ int ko_attention_f32(const float* q, const float* k, const float* v, float* o, i
                      int64_t heads, int64_t head_dim, int64_t q_bstride, int64_t q_row, int64_t k_bstride,
                      int64_t k_row, int64_t v_bstride, int64_t v_row, int64_t o_bstride, int64_t o_row, float scale,
                      int* dev_status, ko_stream_t stream);
+
+/* --- decoder and head steps --------------------------------------------------------------------------------- */
+
+/* out[r][g*128 + k] = sin(v) for even k, cos(v) for odd k, v = ref[r][c_g] * 2*pi / dim_t[k], with coordinates
+ * c_g = (1, 0, 2, 3) for the four groups g (y, x, w, h): ref float32 [rows][4], dim_t float32 [128], out
+ * float32 [rows][512], 16-byte aligned. Replaces sine_embed (fast_rfdetr/model.py:188-194). */
+int ko_sine_embed(const float* ref, const float* dim_t, int64_t rows, float* out, ko_stream_t stream);
+
+/* out = act(x @ w + bias) for narrow outputs, fp32 FMA (not the tensor cores): x float32 [M][K], w float32
+ * [K][N] row-major, bias float32 [N] or NULL, out float32 [M][N]; 1 <= N <= 32, K*N <= 12288, act KO_ACT_NONE or
+ * KO_ACT_RELU. Deterministic (fixed reduction order). Replaces the class heads' matmuls (fast_rfdetr/model.py:179,
+ * :269) and the 4-wide last layer of the encoder's box MLP (:180). */
+int ko_linear_small_f32(const float* x, const float* w, const float* bias, int64_t M, int64_t K, int64_t N,
+                        int act, float* out, ko_stream_t stream);
+
+/* boxes[r] = (d0 * ref2 + ref0, d1 * ref3 + ref1, exp(d2) * ref2, exp(d3) * ref3) with d = x[r] @ w + bias:
+ * the last layer of the box MLP (K inputs, 4 outputs) and the box refinement in one kernel. x float32 [M][K], w
+ * float32 [K][4], bias float32 [4] or NULL, ref float32 [M][4] (cx, cy, w, h), boxes float32 [M][4]; ref and boxes
+ * 16-byte aligned, K <= 3072. Replaces bbox_embed's last layer and the box arithmetic of fast_rfdetr/model.py:270-272. */
+int ko_box_head_f32(const float* x, const float* w, const float* bias, const float* ref, int64_t M, int64_t K,
+                    float* boxes, ko_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -46,14 +46,18 @@ SIGNATURES = {
     "ko_linear_gelu_f32_noalloc": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "ko_attention_f32": (_i32, [_vp, _vp, _vp, _vp] + [_i64] * 12 + [_f32, _vp, _vp]),
     "ko_layernorm": (_i32, [_vp, _vp, _vp, _f32, _i64, _i64, _i32, _vp, _vp]),
-    "ko_linear_residual_ln_f32_packed": (_i32, [_vp] * 7 + [_f32, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp]),
-    "ko_conv3x3_ln_f32_packed": (_i32, [_vp] * 5 + [_f32] + [_i64] * 5 + [_i32, _vp, _vp, _vp]),
+    "ko_linear_residual_ln_f32_packed": (_i32, [_vp] * 7 + [_f32, _i64, _i64, _i64, _i32, _vp, _vp, _i64, _vp, _vp]),
+    "ko_conv3x3_ln_f32_packed": (_i32, [_vp, _i64] + [_vp] * 4 + [_f32] + [_i64] * 5 + [_i32, _vp, _i64, _vp, _vp]),
     "ko_wait_probe": (_i32, [_i64, _vp, _vp]),
     "ko_window_merge_ln": (_i32, [_vp, _vp, _vp, _f32] + [_i64] * 5 + [_i32, _vp, _i64, _i64, _vp]),
     "ko_window_partition_ln": (_i32, [_vp] * 5 + [_f32] + [_i64] * 5 + [_vp, _vp, _vp]),
     "ko_deform_prep": (_i32, [_vp, _vp] + [_i64] * 5 + [_vp, _vp, _vp]),
     "ko_select_queries": (_i32, [_vp] * 5 + [_i64] * 4 + [_vp, _vp, _vp]),
     "ko_im2col3x3": (_i32, [_vp, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "ko_linear_add_f32_packed": (_i32, [_vp] * 4 + [_i64] * 5 + [_i32, _vp, _vp, _vp]),
+    "ko_sine_embed": (_i32, [_vp, _vp, _i64, _vp, _vp]),
+    "ko_linear_small_f32": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp]),
+    "ko_box_head_f32": (_i32, [_vp] * 4 + [_i64, _i64, _vp, _vp]),
 }
 
 _lock = threading.Lock()
@@ -90,7 +94,8 @@ LAUNCHING = {"ko_preprocess": 1, "ko_preprocess_batch": 1, "ko_residual_layernor
              "ko_linear_gelu_f32_noalloc": 2, "ko_attention_f32": 1, "ko_layernorm": 1, "ko_im2col3x3": 1,
              "ko_linear_residual_ln_f32_packed": 1, "ko_select_queries": 1,
              "ko_conv3x3_ln_f32_packed": 1,
-             "ko_wait_probe": 1, "ko_window_merge_ln": 1, "ko_window_partition_ln": 1, "ko_deform_prep": 1}
+             "ko_wait_probe": 1, "ko_window_merge_ln": 1, "ko_window_partition_ln": 1, "ko_deform_prep": 1,
+             "ko_linear_add_f32_packed": 1, "ko_sine_embed": 1, "ko_linear_small_f32": 1, "ko_box_head_f32": 1}
 launch_count: dict[str, int] = {}
 
 

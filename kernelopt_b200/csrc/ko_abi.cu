@@ -121,7 +121,7 @@ extern "C" {
 
 const char* ko_last_error_string(void) { return ko::g_last_error.c_str(); }
 
-int ko_abi_version(void) { return 1; }
+int ko_abi_version(void) { return 2; }
 
 int ko_check_device(void) {
   const ko::DeviceInfo& d = ko::device_info();

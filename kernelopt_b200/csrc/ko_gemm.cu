@@ -119,6 +119,10 @@ struct GemmArgs {
   // x shifted by (ky - 1) * conv_w + (kx - 1) for tap ky * 3 + kx; rows whose shifted pixel lies outside the
   // image are zeroed by the split warps.
   int conv_h, conv_w, conv_c;
+  // EPI_ACT only: out = act(acc + bias + addend) with addend[row * ld_add + col] for col < add_cols (a per-element
+  // term, e.g. the product of a second operand that the caller computed once for several GEMMs), or null
+  const float* addend;
+  int ld_add, add_cols;
 };
 
 // Tiles of one CTA. EPI_ACT: tile t of the m_tiles x n_tiles grid, CTAs strided over tiles. EPI_LN: tile t is
@@ -774,11 +778,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col = col0 + 4 * j;
           float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
           if (args.bias && col < args.N) b = __ldg(reinterpret_cast<const float4*>(args.bias + col));
+          float4 ad = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (args.addend) {
+            const int row = m0 + quad * 32 + lane;
+            if (row < args.M && col < args.add_cols)
+              ad = __ldg(reinterpret_cast<const float4*>(args.addend + static_cast<int64_t>(row) * args.ld_add + col));
+          }
           float4 o;
-          o.x = apply_act(__uint_as_float(r[4 * j + 0]) + b.x, args.act);
-          o.y = apply_act(__uint_as_float(r[4 * j + 1]) + b.y, args.act);
-          o.z = apply_act(__uint_as_float(r[4 * j + 2]) + b.z, args.act);
-          o.w = apply_act(__uint_as_float(r[4 * j + 3]) + b.w, args.act);
+          o.x = apply_act(__uint_as_float(r[4 * j + 0]) + b.x + ad.x, args.act);
+          o.y = apply_act(__uint_as_float(r[4 * j + 1]) + b.y + ad.y, args.act);
+          o.z = apply_act(__uint_as_float(r[4 * j + 2]) + b.z + ad.z, args.act);
+          o.w = apply_act(__uint_as_float(r[4 * j + 3]) + b.w + ad.w, args.act);
           // row `lane` of the tile, 16-byte chunk j, 128-byte swizzle: chunk position j ^ (row % 8)
           *reinterpret_cast<float4*>(stile + lane * 128 + ((j ^ (lane & 7)) << 4)) = o;
         }
@@ -834,8 +844,9 @@ __global__ void __launch_bounds__(256) pack_weight_kernel(const float* __restric
 namespace {
 
 template <int BN, int BKB, bool SPLIT>
-int launch_gemm(const float* x, const float* w_packed, const float* bias, int64_t M, int64_t K, int64_t N,
-                int act, float* out, int* dev_status, cudaStream_t stream) {
+int launch_gemm(const float* x, const float* w_packed, const float* bias, const float* addend, int64_t ld_add,
+                int64_t add_cols, int64_t M, int64_t K, int64_t N, int act, float* out, int* dev_status,
+                cudaStream_t stream) {
   using C = Cfg<BN, BKB, SPLIT, EPI_ACT>;
   const CUtensorMapSwizzle sw = BKB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   CUtensorMap mx, mhi, mlo;
@@ -865,6 +876,9 @@ int launch_gemm(const float* x, const float* w_packed, const float* bias, int64_
   a.N = static_cast<int>(N);
   a.K = static_cast<int>(K);
   a.act = act;
+  a.addend = addend;
+  a.ld_add = static_cast<int>(ld_add);
+  a.add_cols = static_cast<int>(add_cols);
   a.m_tiles = static_cast<int>((M + BM - 1) / BM);
   a.n_tiles = static_cast<int>((N + BN - 1) / BN);
   a.k_blocks = static_cast<int>((K + C::kBK - 1) / C::kBK);
@@ -880,20 +894,22 @@ template <int BN, bool SPLIT>
 int launch_gemm_ln(const float* x, const float* w_packed, const float* bias, const float* scale, const float* resid,
                    const float* gamma, const float* beta, float eps, int64_t M, int64_t K, int64_t N, int act,
                    float* v_out, float* y, int* dev_status, cudaStream_t stream, int conv_h = 0, int conv_w = 0,
-                   int conv_c = 0) {
+                   int conv_c = 0, int64_t ldx = 0, int64_t ldy = 0) {
   constexpr int BKB = 64;
   using C = Cfg<BN, BKB, SPLIT, EPI_LN>;
   const int cs = static_cast<int>(N / BN);
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_64B;
   CUtensorMap mx, mhi, mlo, my, mv;
   const int64_t xcols = conv_c > 0 ? conv_c : K;  // an implicit convolution reads x as [M][C]
-  int st = ko::make_tmap_2d_f32(&mx, x, M, xcols, xcols, BM, C::kBK, sw, "ko_linear_residual_ln x");
+  if (ldx == 0) ldx = xcols;                       // row pitches of x and y (0: dense rows)
+  if (ldy == 0) ldy = N;
+  int st = ko::make_tmap_2d_f32(&mx, x, M, xcols, ldx, BM, C::kBK, sw, "ko_linear_residual_ln x");
   if (st) return st;
   st = ko::make_tmap_2d_f32(&mhi, w_packed, N, K, K, BN, C::kBK, sw, "ko_linear_residual_ln w_hi");
   if (st) return st;
   st = ko::make_tmap_2d_f32(&mlo, w_packed + N * K, N, K, K, BN, C::kBK, sw, "ko_linear_residual_ln w_lo");
   if (st) return st;
-  st = ko::make_tmap_2d_f32(&my, y, M, N, N, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, "ko_linear_residual_ln y");
+  st = ko::make_tmap_2d_f32(&my, y, M, N, ldy, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, "ko_linear_residual_ln y");
   if (st) return st;
   st = ko::make_tmap_2d_f32(&mv, v_out ? v_out : y, M, N, N, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B,
                             "ko_linear_residual_ln h_out");
@@ -969,7 +985,8 @@ int launch_gemm_ln(const float* x, const float* w_packed, const float* bias, con
   return ko::check_launch("ko_linear_residual_ln_f32_packed");
 }
 
-using LaunchFn = int (*)(const float*, const float*, const float*, int64_t, int64_t, int64_t, int, float*, int*,
+using LaunchFn = int (*)(const float*, const float*, const float*, const float*, int64_t, int64_t, int64_t, int64_t,
+                         int64_t, int, float*, int*,
                          cudaStream_t);
 
 struct Variant {
@@ -1071,13 +1088,34 @@ extern "C" int ko_linear_f32_packed(const float* x, const float* w_packed, const
   st = ko::device_or_fail(&info, "ko_linear_f32_packed");
   if (st) return st;
   const Variant* v = choose_variant(M, N, K, info->sm_count);
-  return v->fn(x, w_packed, bias, M, K, N, act, out, dev_status, reinterpret_cast<cudaStream_t>(stream));
+  return v->fn(x, w_packed, bias, nullptr, 0, 0, M, K, N, act, out, dev_status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ko_linear_add_f32_packed(const float* x, const float* w_packed, const float* bias, const float* addend,
+                                        int64_t ld_addend, int64_t add_cols, int64_t M, int64_t K, int64_t N, int act,
+                                        float* out, int* dev_status, ko_stream_t stream) {
+  const char* who = "ko_linear_add_f32_packed";
+  int st = validate_linear(x, w_packed, bias, M, K, N, out, who);
+  if (st || M == 0) return st;
+  if (act != KO_ACT_NONE && act != KO_ACT_GELU && act != KO_ACT_RELU)
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": unknown activation");
+  if (!addend || !ko::aligned16(addend) || add_cols < 4 || add_cols > N || add_cols % 4 != 0 || ld_addend < add_cols ||
+      ld_addend % 4 != 0 || ld_addend > INT32_MAX || M * ld_addend > (int64_t(1) << 40))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": addend must be 16-byte aligned, 4 <= add_cols <= N, "
+                                                                "add_cols and ld_addend multiples of 4, ld >= add_cols");
+  if (addend == out) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": out must not alias addend");
+  const ko::DeviceInfo* info = nullptr;
+  st = ko::device_or_fail(&info, who);
+  if (st) return st;
+  const Variant* v = choose_variant(M, N, K, info->sm_count);
+  return v->fn(x, w_packed, bias, addend, ld_addend, add_cols, M, K, N, act, out, dev_status,
+               reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ko_linear_residual_ln_f32_packed(const float* x, const float* w_packed, const float* bias,
                                                 const float* scale, const float* resid, const float* gamma,
                                                 const float* beta, float eps, int64_t M, int64_t K, int64_t N,
-                                                int act, float* h_out, float* y, int* dev_status,
+                                                int act, float* h_out, float* y, int64_t ldy, int* dev_status,
                                                 ko_stream_t stream) {
   const char* who = "ko_linear_residual_ln_f32_packed";
   int st = validate_linear(x, w_packed, bias, M, K, N, y, who);
@@ -1094,6 +1132,8 @@ extern "C" int ko_linear_residual_ln_f32_packed(const float* x, const float* w_p
     return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": pointers must be 16-byte aligned");
   if (y == resid || y == h_out || y == x)
     return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": y must not alias x, resid or h_out");
+  if (ldy != 0 && (ldy < N || ldy % 4 != 0 || ldy > INT32_MAX))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": ldy must be 0 or a multiple of 4 >= N");
   const ko::DeviceInfo* info = nullptr;
   st = ko::device_or_fail(&info, who);
   if (st) return st;
@@ -1111,9 +1151,9 @@ extern "C" int ko_linear_residual_ln_f32_packed(const float* x, const float* w_p
 #define KO_LN_CASE(BNV)                                                                                         \
   if (bn == BNV)                                                                                               \
     return split ? launch_gemm_ln<BNV, true>(x, w_packed, bias, scale, resid, gamma, beta, eps, M, K, N, act,   \
-                                             h_out, y, dev_status, s)                                          \
+                                             h_out, y, dev_status, s, 0, 0, 0, 0, ldy)                         \
                  : launch_gemm_ln<BNV, false>(x, w_packed, bias, scale, resid, gamma, beta, eps, M, K, N, act,  \
-                                              h_out, y, dev_status, s);
+                                              h_out, y, dev_status, s, 0, 0, 0, 0, ldy);
   KO_LN_CASE(128)
   KO_LN_CASE(192)
   KO_LN_CASE(256)
@@ -1121,9 +1161,10 @@ extern "C" int ko_linear_residual_ln_f32_packed(const float* x, const float* w_p
   return ko::fail(KO_ERR_UNSUPPORTED, std::string(who) + ": no tile for this N");
 }
 
-extern "C" int ko_conv3x3_ln_f32_packed(const float* x, const float* w_packed, const float* bias, const float* gamma,
-                                        const float* beta, float eps, int64_t B, int64_t H, int64_t W, int64_t C,
-                                        int64_t N, int act, float* y, int* dev_status, ko_stream_t stream) {
+extern "C" int ko_conv3x3_ln_f32_packed(const float* x, int64_t ldx, const float* w_packed, const float* bias,
+                                        const float* gamma, const float* beta, float eps, int64_t B, int64_t H,
+                                        int64_t W, int64_t C, int64_t N, int act, float* y, int64_t ldy,
+                                        int* dev_status, ko_stream_t stream) {
   const char* who = "ko_conv3x3_ln_f32_packed";
   if (B < 0 || H < 1 || W < 1 || C < 16 || C % 16 != 0 || B * H * W > INT32_MAX || C > 4096)
     return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": need C % 16 == 0 and a batch below 2^31 pixels");
@@ -1137,6 +1178,9 @@ extern "C" int ko_conv3x3_ln_f32_packed(const float* x, const float* w_packed, c
   if (!gamma || !beta || !(eps >= 0.0f) || !ko::aligned16(gamma) || !ko::aligned16(beta))
     return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": gamma, beta required and 16-byte aligned; eps >= 0");
   if (y == x) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": y must not alias x");
+  if ((ldx != 0 && (ldx < C || ldx % 4 != 0 || ldx > INT32_MAX)) ||
+      (ldy != 0 && (ldy < N || ldy % 4 != 0 || ldy > INT32_MAX)))
+    return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": ldx / ldy must be 0 or multiples of 4 >= C / N");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool split = K > KO_SPLIT_MIN_K;
   const int bn = N == 384 ? 192 : N == 512 ? 256 : static_cast<int>(N);
@@ -1144,9 +1188,9 @@ extern "C" int ko_conv3x3_ln_f32_packed(const float* x, const float* w_packed, c
 #define KO_CONV_CASE(BNV)                                                                                        \
   if (bn == BNV)                                                                                                \
     return split ? launch_gemm_ln<BNV, true>(x, w_packed, bias, nullptr, nullptr, gamma, beta, eps, M, K, N, act, \
-                                             nullptr, y, dev_status, s, h, w, c)                                  \
+                                             nullptr, y, dev_status, s, h, w, c, ldx, ldy)                        \
                  : launch_gemm_ln<BNV, false>(x, w_packed, bias, nullptr, nullptr, gamma, beta, eps, M, K, N, act,\
-                                              nullptr, y, dev_status, s, h, w, c);
+                                              nullptr, y, dev_status, s, h, w, c, ldx, ldy);
   KO_CONV_CASE(128)
   KO_CONV_CASE(192)
   KO_CONV_CASE(256)

@@ -132,20 +132,7 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(const __grid_const
 // overlap the arithmetic of this one. Per output element the loop does 4 byte loads from shared memory, the
 // integer tap arithmetic, one LUT load from shared memory and a quarter of a 128-bit store.
 // ---------------------------------------------------------------------------------------------------------
-// Threads per band CTA (measurement builds may override it: -DKO_PRE_BAND_THREADS=n, a multiple of 32 <= 1024).
-#ifndef KO_PRE_BAND_THREADS
-#define KO_PRE_BAND_THREADS 256
-#endif
-constexpr int kBandThreads = KO_PRE_BAND_THREADS;
-// Copies of the normalisation LUT in shared memory: lane i reads copy i % kLutCopies, so a warp's 32 lookups of
-// random 8-bit values spread over kLutCopies banks instead of colliding in the bank of each value (32 copies:
-// every lane has a bank of its own, one wavefront per lookup; one copy: ~3.5 wavefronts for random values).
-// Measurement builds may override it (-DKO_PRE_LUT_COPIES=n, a power of two <= 32).
-#ifndef KO_PRE_LUT_COPIES
-#define KO_PRE_LUT_COPIES 1
-#endif
-constexpr int kLutCopies = KO_PRE_LUT_COPIES;
-static_assert(kLutCopies >= 1 && kLutCopies <= 32 && (kLutCopies & (kLutCopies - 1)) == 0, "LUT copies");
+constexpr int kBandThreads = 256;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(kodev::smem_addr(smem)), "l"(gmem) : "memory");
@@ -160,11 +147,10 @@ __device__ __forceinline__ int64_t row_term(int layout, int y, int dst) {
   return static_cast<int64_t>(y >> 4) * (dst >> 4) * 768 + (y & 15) * 48;  // PATCH16
 }
 
-// The 4 outputs of one item from the staged rows s0 (top) and s1 (bottom). lbase[j]: the element's LUT channel
-// base in the replicated table, (channel * 256) * kLutCopies + this lane's copy.
+// The 4 outputs of one item from the staged rows s0 (top) and s1 (bottom).
 template <int MODE>
 __device__ __forceinline__ float4 item_values(const uint8_t* s0, const uint8_t* s1, const int4 (&tap)[4],
-                                              const int (&lbase)[4], int4 yt, const float* slut) {
+                                              uint32_t chans, int4 yt, const float* slut) {
   float v[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -181,7 +167,7 @@ __device__ __forceinline__ float4 item_values(const uint8_t* s0, const uint8_t* 
       q = ((((h0 >> 4) * yt.z) >> 16) + (((h1 >> 4) * yt.w) >> 16) + 2) >> 2;
     }
     q = min(max(q, 0), 255);
-    v[j] = slut[lbase[j] + q * kLutCopies];
+    v[j] = slut[(((chans >> (2 * j)) & 3u) << 8) + q];  // RGB channel of element j: 2 bits each
   }
   return make_float4(v[0], v[1], v[2], v[3]);
 }
@@ -192,8 +178,8 @@ __global__ void __launch_bounds__(kBandThreads) preprocess_band_kernel(const __g
                                                                        int layout, float* __restrict__ out,
                                                                        int row_cap, int band) {
   extern __shared__ __align__(16) uint8_t smem[];
-  float* slut = reinterpret_cast<float*>(smem);   // [3][256][kLutCopies]
-  uint8_t* rowbuf = smem + 768 * 4 * kLutCopies;  // [3 buffers][2 rows][row_cap]
+  float* slut = reinterpret_cast<float*>(smem);  // [3][256]
+  uint8_t* rowbuf = smem + 768 * 4;              // [3 buffers][2 rows][row_cap]
   const ImageParams& im = p.img[blockIdx.y];
   const int tid = threadIdx.x;
   const int y_begin = blockIdx.x * band;
@@ -234,13 +220,11 @@ __global__ void __launch_bounds__(kBandThreads) preprocess_band_kernel(const __g
   };
 
   int4 yt_next = stage(y_begin, 0);
-  for (int i = tid; i < 768 * kLutCopies; i += kBandThreads) slut[i] = __ldg(lut + i / kLutCopies);
-  const int copy = tid & (kLutCopies - 1);
+  for (int i = tid; i < 768; i += kBandThreads) slut[i] = __ldg(lut + i);
 
   // Per-thread column set-up: clamped taps (l, r), weights, RGB channel and output column offset of each element.
   int4 tap[IPT][4];
   uint32_t chans[IPT];
-  int lbase[IPT][4];
   float* obase[IPT];
   bool live[IPT];
 #pragma unroll
@@ -281,8 +265,6 @@ __global__ void __launch_bounds__(kBandThreads) preprocess_band_kernel(const __g
         tap[k][j].y = min(max(tap[k][j].y, 0), last);
       }
     }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) lbase[k][j] = static_cast<int>((chans[k] >> (2 * j)) & 3u) * 256 * kLutCopies + copy;
     obase[k] = out + img_base + col_off;
   }
 
@@ -303,8 +285,8 @@ __global__ void __launch_bounds__(kBandThreads) preprocess_band_kernel(const __g
 #pragma unroll
     for (int k = 0; k < IPT; ++k) {
       if (!live[k]) continue;
-      const float4 v = mode == 0 ? item_values<0>(s0, s1, tap[k], lbase[k], yt, slut)
-                                 : item_values<1>(s0, s1, tap[k], lbase[k], yt, slut);
+      const float4 v = mode == 0 ? item_values<0>(s0, s1, tap[k], chans[k], yt, slut)
+                                 : item_values<1>(s0, s1, tap[k], chans[k], yt, slut);
       *reinterpret_cast<float4*>(obase[k] + rt) = v;
     }
   }
@@ -360,7 +342,7 @@ extern "C" int ko_preprocess_batch(const ko_image_desc* images, int n, const flo
     const int64_t target = 8 * static_cast<int64_t>(info.sm_count);
     int band = 16;
     while (band > 1 && n * ((dst + band - 1) / band) < target) band /= 2;
-    const int64_t smem = 768 * 4 * kLutCopies + 6 * row_cap;
+    const int64_t smem = 768 * 4 + 6 * row_cap;
     if (smem > info.max_smem_optin) return ko::fail(KO_ERR_INVALID_ARGUMENT, "ko_preprocess: source rows too wide");
     dim3 grid(static_cast<unsigned>((dst + band - 1) / band), static_cast<unsigned>(n));
     auto kern = n_items <= kBandThreads ? preprocess_band_kernel<1> : preprocess_band_kernel<2>;

@@ -321,6 +321,79 @@ def linear(x, pw: PackedWeight, act=None, out=None):
     return out
 
 
+def linear_add(x, pw: PackedWeight, addend, act=None, out=None):
+    """act(x @ W + bias + addend) in one GEMM: addend [..., add_cols] (add_cols <= N, a multiple of 4) is added to
+    the first add_cols output columns in the epilogue; its last dimension must be contiguous (any row stride, a
+    multiple of 4), e.g. a column slice of a wider precomputed product. The decoder's (tgt + qpos) @ W =
+    tgt @ W + qpos @ W (fast_rfdetr/model.py:251, :256) with qpos @ W computed once for all layers."""
+    _need(x, "x")
+    if x.shape[-1] != pw.k:
+        raise ValueError(f"x has {x.shape[-1]} features, the weight expects {pw.k}")
+    if not isinstance(addend, torch.Tensor) or not addend.is_cuda or addend.dtype != torch.float32 \
+            or addend.dim() != 2 or addend.stride(1) != 1:
+        raise ValueError("addend must be a float32 CUDA [M, add_cols] tensor with a contiguous last dimension")
+    m = x.numel() // pw.k
+    if addend.shape[0] != m:
+        raise ValueError(f"addend has {addend.shape[0]} rows, x has {m}")
+    if out is None:
+        out = torch.empty((*x.shape[:-1], pw.n), dtype=torch.float32, device=x.device)
+    call("ko_linear_add_f32_packed", x.data_ptr(), pw.packed.data_ptr(), _ptr(pw.bias), addend.data_ptr(),
+         addend.stride(0), addend.shape[1], m, pw.k, pw.n, ACTS[act], out.data_ptr(), status_word(x.device).data_ptr(),
+         _stream())
+    return out
+
+
+def sine_embed(ref, dim_t, out=None):
+    """ref [..., 4] (cx, cy, w, h) -> [..., 512]: the sine embedding of the (y, x, w, h) coordinates with the
+    frequency divisors dim_t [128] (fast_rfdetr/model.py:188-194) in one kernel."""
+    _need(ref, "ref")
+    _need(dim_t, "dim_t")
+    if ref.shape[-1] != 4 or dim_t.numel() != 128:
+        raise ValueError("ref must be [..., 4] and dim_t [128]")
+    rows = ref.numel() // 4
+    if out is None:
+        out = torch.empty((*ref.shape[:-1], 512), dtype=torch.float32, device=ref.device)
+    call("ko_sine_embed", ref.data_ptr(), dim_t.data_ptr(), rows, out.data_ptr(), _stream())
+    return out
+
+
+def linear_small(x, w, bias=None, act=None):
+    """act(x @ w + bias) for narrow outputs (N <= 32; the 11-class and 4-wide heads) on fp32 FMA: x [..., K],
+    w [K, N] row-major, bias [N] or None, act None or 'relu'."""
+    _need(x, "x")
+    _need(w, "w")
+    k, n = w.shape
+    if x.shape[-1] != k:
+        raise ValueError(f"x has {x.shape[-1]} features, the weight expects {k}")
+    if bias is not None and _need(bias, "bias").numel() != n:
+        raise ValueError(f"bias must have {n} elements")
+    if act not in (None, "none", "relu"):
+        raise ValueError("act must be None or 'relu'")
+    out = torch.empty((*x.shape[:-1], n), dtype=torch.float32, device=x.device)
+    call("ko_linear_small_f32", x.data_ptr(), w.data_ptr(), _ptr(bias), x.numel() // k, k, n, ACTS[act],
+         out.data_ptr(), _stream())
+    return out
+
+
+def box_head(x, w, bias, ref):
+    """Boxes from the box MLP's last layer and the reference boxes: d = x @ w + bias (w [K, 4]), then
+    (d0 * r2 + r0, d1 * r3 + r1, exp(d2) * r2, exp(d3) * r3) with r = ref [..., 4] (fast_rfdetr/model.py:270-272)."""
+    _need(x, "x")
+    _need(w, "w")
+    _need(ref, "ref")
+    k = w.shape[0]
+    if tuple(w.shape) != (k, 4) or x.shape[-1] != k:
+        raise ValueError("w must be [K, 4] and x [..., K]")
+    if tuple(ref.shape) != (*x.shape[:-1], 4):
+        raise ValueError("ref must be [..., 4] with the rows of x")
+    if bias is not None and _need(bias, "bias").numel() != 4:
+        raise ValueError("bias must have 4 elements")
+    out = torch.empty((*x.shape[:-1], 4), dtype=torch.float32, device=x.device)
+    call("ko_box_head_f32", x.data_ptr(), w.data_ptr(), _ptr(bias), ref.data_ptr(), x.numel() // k, k, out.data_ptr(),
+         _stream())
+    return out
+
+
 def select_queries(logits, delta, proposals, rp_xy, rp_ewh, nq, ref=None, idx=None):
     """The reference's query selection (model.py:175-185) in one kernel: per frame the nq proposals with the
     highest class score (max over the last dimension of logits; ties by ascending index), and their reference
@@ -351,8 +424,9 @@ def linear_residual_layernorm(x, pw: PackedWeight, gamma, beta, eps, resid=None,
     """One GEMM with the residual add and LayerNorm in its epilogue:
         h_out = resid + (x @ W + bias) * scale;   y = act(LayerNorm(h_out) * gamma + beta)
     bias is the PackedWeight's (None = 0), scale None = 1, resid None = no residual, act None or 'silu'.
-    Returns (h_out, y); h_out is None when write_h is False. h_out may be resid (in place). W's width must be
-    one of LN_WIDTHS. Fuses the reference's out-projection / fc2 GEMM + residual_layernorm pairs
+    Returns (h_out, y); h_out is None when write_h is False. h_out may be resid (in place). y may be given as a
+    column slice of a wider buffer (last dimension contiguous, rows any multiple of 4 floats apart). W's width
+    must be one of LN_WIDTHS. Fuses the reference's out-projection / fc2 GEMM + residual_layernorm pairs
     (model.py:121-123, 129-132) and the projector's conv GEMM + LayerNorm + SiLU (model.py:148-158)."""
     _need(x, "x")
     if x.shape[-1] != pw.k:
@@ -371,24 +445,44 @@ def linear_residual_layernorm(x, pw: PackedWeight, gamma, beta, eps, resid=None,
     m = x.numel() // pw.k
     if y is None:
         y = torch.empty(shape, dtype=torch.float32, device=x.device)
+    ldy = _row_pitch(y, m, n, "y")
     if write_h and h_out is None:
         h_out = torch.empty(shape, dtype=torch.float32, device=x.device)
     call("ko_linear_residual_ln_f32_packed", x.data_ptr(), pw.packed.data_ptr(), _ptr(pw.bias), _ptr(scale),
          _ptr(resid), gamma.data_ptr(), beta.data_ptr(), float(eps), m, pw.k, n,
          _lib.KO_ACT_SILU if act == "silu" else _lib.KO_ACT_NONE, _ptr(h_out if write_h else None), y.data_ptr(),
-         status_word(x.device).data_ptr(), _stream())
+         ldy, status_word(x.device).data_ptr(), _stream())
     return (h_out if write_h else None), y
+
+
+def _row_pitch(t, rows: int, cols: int, name: str) -> int:
+    """Elements between consecutive rows of t viewed as [rows, cols] (its last dimension contiguous, its rows
+    evenly spaced): a dense tensor or a column slice of a wider one."""
+    if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.float32:
+        raise ValueError(f"{name} must be a float32 CUDA tensor")
+    if t.dim() < 2 or t.shape[-1] != cols or t.numel() != rows * cols or t.stride(-1) != 1:
+        raise ValueError(f"{name} must hold [{rows}, {cols}] with a contiguous last dimension")
+    pitch = t.stride(-2)
+    step = pitch
+    for d in range(t.dim() - 2, -1, -1):  # every leading dimension steps by whole rows
+        if t.shape[d] > 1 and t.stride(d) != step:
+            raise ValueError(f"{name}: rows are not evenly spaced")
+        step *= t.shape[d]
+    if pitch < cols or pitch % 4:
+        raise ValueError(f"{name}: row pitch {pitch} must be a multiple of 4 and at least {cols}")
+    return pitch
 
 
 def conv3x3_layernorm(x, pw: PackedWeight, gamma, beta, eps, act=None, out=None):
     """act(LayerNorm(conv3x3(x) + bias) * gamma + beta) for an NHWC float32 x [B, H, W, C] (C % 16 == 0): the
     3x3 / stride 1 / padding 1 convolution as an implicit GEMM (no im2col buffer) with the LayerNorm epilogue.
-    pw: the weight as [9*C, N] in (ky, kx, c) row order (PackedWeight; its bias is the conv bias). Returns
-    [B*H*W, N]. The projector's conv -> channel LayerNorm -> SiLU block (model.py:148-158) in one kernel."""
-    _need(x, "x")
+    pw: the weight as [9*C, N] in (ky, kx, c) row order (PackedWeight; its bias is the conv bias). Returns out,
+    [B*H*W, N] (or the [B, H, W, N] channel slice of a wider NHWC buffer given as `out`). x may be a channel slice
+    of a wider NHWC buffer too. The projector's conv -> channel LayerNorm -> SiLU block (model.py:148-158)."""
     if x.dim() != 4:
         raise ValueError("x must be [B, H, W, C]")
     b, h, w, c = x.shape
+    ldx = _row_pitch(x, b * h * w, c, "x")
     if pw.k != 9 * c:
         raise ValueError(f"the weight has {pw.k} rows, a 3x3 convolution over {c} channels needs {9 * c}")
     if pw.n not in LN_WIDTHS:
@@ -400,9 +494,10 @@ def conv3x3_layernorm(x, pw: PackedWeight, gamma, beta, eps, act=None, out=None)
         raise ValueError("act must be None or 'silu'")
     if out is None:
         out = torch.empty((b * h * w, pw.n), dtype=torch.float32, device=x.device)
-    call("ko_conv3x3_ln_f32_packed", x.data_ptr(), pw.packed.data_ptr(), _ptr(pw.bias), gamma.data_ptr(),
+    ldy = _row_pitch(out, b * h * w, pw.n, "out")
+    call("ko_conv3x3_ln_f32_packed", x.data_ptr(), ldx, pw.packed.data_ptr(), _ptr(pw.bias), gamma.data_ptr(),
          beta.data_ptr(), float(eps), b, h, w, c, pw.n, _lib.KO_ACT_SILU if act == "silu" else _lib.KO_ACT_NONE,
-         out.data_ptr(), status_word(x.device).data_ptr(), _stream())
+         out.data_ptr(), ldy, status_word(x.device).data_ptr(), _stream())
     return out
 
 

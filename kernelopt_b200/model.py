@@ -10,15 +10,15 @@ Call sites of the reference's kernels (model.py:122, 125, 131, 226) use the same
   deform_attn          decoder cross-attention sampling, on the one fused [B,1600,1024] value projection
 Every other dense layer (QKV, out-proj, fc2, the patch embedding, the projector's 1x1 convs, the decoder
 linears) runs on the same fp32-grade tcgen05 GEMM. The projector's 3x3 convs run on it as an implicit GEMM with
-LayerNorm + SiLU in the epilogue (im2col + GEMM for other widths). Only the layers whose output width is not a
-multiple of 4 (11 classes, 4 box coordinates) use torch's fp32 matmul. Attention — the backbone's windowed and
-global self-attention and the decoder's self-attention (the reference's mx.fast.scaled_dot_product_attention) — runs
-on the fp32-grade 3xTF32 tcgen05 flash-attention kernel, straight on column slices of the fused QKV projection,
-softmax included. The backbone's entry (pos add, windows, class token, first LayerNorm) and each tapped layer's
-merge + LayerNorm are one kernel each. LayerNorms not fused into a GEMM run on the LayerNorm kernel. The top-300
-query selection is one kernel, and so is the sampler's input step (locations + point softmax). What stays in torch
-is glue (the sine embedding of the query boxes, tgt + qpos, the heads' narrow outputs), in fp32 with TF32
-disabled.
+LayerNorm + SiLU in the epilogue, and its C2f concatenation is written in place (each block's output lands in its
+channel slice of one buffer). The heads' 11- and 4-wide outputs run on a narrow fp32 kernel, the box refinement
+fused into the last box layer. Attention — the backbone's windowed and global self-attention and the decoder's
+self-attention (the reference's mx.fast.scaled_dot_product_attention) — runs on the fp32-grade 3xTF32 tcgen05
+flash-attention kernel, straight on column slices of the fused QKV projection, softmax included. The backbone's
+entry (pos add, windows, class token, first LayerNorm) and each tapped layer's merge + LayerNorm are one kernel
+each. The top-300 query selection is one kernel, and so are the sine embedding and the sampler's input step
+(locations + point softmax). The decoder's `tgt + qpos` (model.py:251, :256) becomes tgt @ W + qpos @ W: one GEMM
+per forward computes qpos @ W for all four layers and each layer's GEMM adds its slice in the epilogue.
 
 The input is the patch layout the preprocessing kernel writes (PATCH16: [B, 1600, 768]), which makes the
 16x16/16 patch-embedding convolution one GEMM; NHWC [B, 640, 640, 3] (the reference's input) is accepted too.
@@ -30,7 +30,6 @@ import math
 
 import numpy as np
 import torch
-import torch.nn.functional as F
 
 from . import kernels as K
 from .weights import BB, CA_HEADS, CA_POINTS, DEC, LAYER, PROJ
@@ -49,15 +48,17 @@ def configure_numerics() -> None:
 
 
 class Dense:
-    """A linear layer x @ W + b: tcgen05 3xTF32 GEMM when the output width allows it, else torch fp32."""
+    """A linear layer x @ W + b: the tcgen05 3xTF32 GEMM when the widths are multiples of 4, the narrow-output
+    fp32 kernel (ko_linear_small_f32) for the heads' 11- and 4-wide outputs."""
 
     def __init__(self, w: torch.Tensor, b: torch.Tensor | None):
         self.k, self.n = w.shape
         self.native = self.n % 4 == 0 and self.k % 4 == 0
+        self.w, self.b = w.contiguous(), (None if b is None else b.contiguous())
         if self.native:
-            self.pw = K.pack_weight(w.contiguous(), None if b is None else b.contiguous())
-        else:
-            self.w, self.b = w.contiguous(), b
+            self.pw = K.pack_weight(self.w, self.b)
+        elif not (self.n <= 32 and self.k * self.n <= 12288):
+            raise ValueError(f"no kernel for a {self.k} x {self.n} linear layer")
 
     def ln(self, x: torch.Tensor, ln, resid=None, scale=None, act=None, write_h=None):
         """(h_out, y) with h_out = resid + (x @ W + b) * scale and y = act(LayerNorm(h_out)): one GEMM whose
@@ -80,17 +81,13 @@ class Dense:
         h_out, y = K.residual_layernorm(h.contiguous(), o.contiguous(), None, scale, w, b, eps)
         return h_out, (K.layernorm(h_out, w, b, eps, act) if act else y)
 
-    def __call__(self, x: torch.Tensor, act=None) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, act=None, addend=None) -> torch.Tensor:
+        """act(x @ W + b [+ addend on the first addend.shape[-1] columns])."""
+        if addend is not None:
+            return K.linear_add(x.contiguous(), self.pw, addend, act)
         if self.native:
             return K.linear(x.contiguous(), self.pw, act)
-        y = x @ self.w
-        if self.b is not None:
-            y = y + self.b
-        if act == "relu":
-            y = torch.relu(y)
-        elif act == "gelu":
-            y = F.gelu(y)
-        return y
+        return K.linear_small(x.contiguous(), self.w, self.b, act)
 
 
 class RFDETR:
@@ -156,6 +153,14 @@ class RFDETR:
         self.enc_class = d("transformer.enc_out_class_embed.0")
         self.enc_bbox = [d(f"transformer.enc_out_bbox_embed.0.layers.{j}") for j in range(3)]
         self.valid = p["proposal_valid"]
+        # Masked proposals (valid = 0) enter the encoder head as zero rows, whose output is the same constant row
+        # for every frame: LayerNorm(enc_output(0)). It is computed once here; the per-frame mask multiply of the
+        # reference (model.py:177) then becomes a copy of that row into the masked rows, and nothing at all for
+        # weights whose proposals are all valid (the reference's own).
+        self.masked = torch.nonzero(self.valid[:, 0] == 0)[:, 0]
+        self.enc_zero_row = None
+        if self.masked.numel():
+            _, self.enc_zero_row = self.enc_output.ln(torch.zeros((1, D_MODEL), device=dev), self.enc_norm)
         self.props = p["proposals"]
         rp = p["refpoint_embed"]
         self.rp_xy, self.rp_ewh = rp[:, :2].contiguous(), torch.exp(rp[:, 2:]).contiguous()
@@ -164,19 +169,28 @@ class RFDETR:
         self.rph = [d(DEC + f"ref_point_head.layers.{j}") for j in range(2)]
         vp = [DEC + f"layers.{i}.cross_attn.value_proj" for i in range(4)]
         self.vproj = Dense(torch.cat([p[k + ".weight"] for k in vp], 1), torch.cat([p[k + ".bias"] for k in vp]))
+        # (tgt + qpos) @ W = tgt @ W + qpos @ W: qpos is the same in all four layers, so its products with each
+        # layer's q | k and offset | weight projections come from one GEMM per forward ([rows, 4 * 608]), which
+        # the layers' GEMMs of tgt add in their epilogues; the value projection of tgt joins the q | k GEMM.
         self.dec = []
+        pos_w = []
         for i in range(4):
             pre = DEC + f"layers.{i}."
             sa = pre + "self_attn."
             wqk = torch.cat([p[sa + "q.weight"], p[sa + "k.weight"]], 1)
-            bqk = torch.cat([p[sa + "q.bias"], p[sa + "k.bias"]])
+            wqkv = torch.cat([wqk, p[sa + "v.weight"]], 1)
+            bqkv = torch.cat([p[sa + "q.bias"], p[sa + "k.bias"], p[sa + "v.bias"]])
             ca = pre + "cross_attn."
             woff = torch.cat([p[ca + "sampling_offsets.weight"], p[ca + "attention_weights.weight"]], 1)
             boff = torch.cat([p[ca + "sampling_offsets.bias"], p[ca + "attention_weights.bias"]])
+            pos_w += [wqk, woff]
             self.dec.append(dict(
-                qk=Dense(wqk, bqk), v=d(sa + "v"), out=d(sa + "out_proj"), norm1=self._ln(pre + "norm1"),
+                qkv=Dense(wqkv, bqkv), out=d(sa + "out_proj"), norm1=self._ln(pre + "norm1"),
                 offaw=Dense(woff, boff), oproj=d(ca + "output_proj"), norm2=self._ln(pre + "norm2"),
                 l1=d(pre + "linear1"), l2=d(pre + "linear2"), norm3=self._ln(pre + "norm3")))
+        self.pos_proj = Dense(torch.cat(pos_w, 1), None)                      # [256, 4 * (512 + 96)]
+        self.pos_cols = 2 * D_MODEL + woff.shape[1]                            # 608 columns per layer
+        self._tgt0: dict[int, torch.Tensor] = {}
         self.dec_norm = self._ln(DEC + "norm")
         self.class_embed = d("class_embed")
         self.bbox_embed = [d(f"bbox_embed.layers.{j}") for j in range(3)]
@@ -220,27 +234,34 @@ class RFDETR:
         return lyr["fc2"].ln(m, lyr["next_norm"], resid=h, scale=lyr["ls2"])
 
     # ---- projector ----------------------------------------------------------------------------------------
-    def _convx(self, x, cv):
-        """conv (as GEMM; 3x3 through im2col) + channel LayerNorm + SiLU (model.py:148-158)."""
+    def _convx(self, x, cv, out=None):
+        """conv (1x1 as GEMM, 3x3 as implicit GEMM) + channel LayerNorm + SiLU (model.py:148-158) in one kernel.
+        x may be a channel slice of a wider NHWC buffer, and `out` ([B, H, W, N], possibly such a slice) receives
+        the result; returns it."""
         b, hh, ww, cin = x.shape
         dense = cv["dense"]
+        w, bt, eps = cv["ln"]
+        if out is None:
+            out = x.new_empty((b, hh, ww, dense.n))
         if cv["k"] == 1:
-            cols = x.reshape(b * hh * ww, cin)
-        elif dense.native and dense.n in K.LN_WIDTHS and cin % 16 == 0:
-            w, bt, eps = cv["ln"]                                  # implicit-GEMM conv + LN + SiLU, one kernel
-            return K.conv3x3_layernorm(x.contiguous(), dense.pw, w, bt, eps, "silu").reshape(b, hh, ww, -1)
+            K.linear_residual_layernorm(x.reshape(b * hh * ww, cin), dense.pw, w, bt, eps, act="silu", y=out,
+                                        write_h=False)
         else:
-            cols = K.im2col3x3(x.contiguous())                                                   # [B*H*W, 9*cin]
-        _, y = dense.ln(cols, cv["ln"], act="silu")                                           # GEMM + LN + SiLU
-        return y.reshape(b, hh, ww, -1)
+            K.conv3x3_layernorm(x, dense.pw, w, bt, eps, "silu", out=out)
+        return out
 
     def projector(self, feats):
-        """feats: the backbone's concatenated feature maps [B, 40, 40, 4C] -> [B, 40, 40, 256] (model.py:148-167)."""
-        y = self._convx(feats, self.cv1)
-        parts = [y[..., :128], y[..., 128:]]
-        for cv_a, cv_b in self.bottlenecks:
-            parts.append(self._convx(self._convx(parts[-1].contiguous(), cv_a), cv_b))
-        y = self._convx(torch.cat(parts, -1), self.cv2)
+        """feats: the backbone's concatenated feature maps [B, 40, 40, 4C] -> [B, 40, 40, 256] (model.py:148-167).
+        The C2f concatenation (model.py:161-162) is never copied: cv1 writes channels [0, 256) of one
+        [B, 40, 40, 640] buffer, each bottleneck reads the previous 128-channel slice in place and writes the next
+        slice, and cv2 reads the whole buffer."""
+        b = feats.shape[0]
+        cat = feats.new_empty((b, GRID, GRID, 128 * (2 + len(self.bottlenecks))))
+        self._convx(feats, self.cv1, out=cat[..., :256])
+        for j, (cv_a, cv_b) in enumerate(self.bottlenecks):
+            t = self._convx(cat[..., 128 * (j + 1):128 * (j + 2)], cv_a)
+            self._convx(t, cv_b, out=cat[..., 128 * (j + 2):128 * (j + 3)])
+        y = self._convx(cat, self.cv2)
         return self._ln_op(y, self.proj_ln)
 
     # ---- query selection ------------------------------------------------------------------------------------
@@ -253,8 +274,9 @@ class RFDETR:
         """model.py:175-185: class score per proposal, box refinement, top-300 by score. The score maximum, the
         ranking (ties by ascending proposal index), the gather and the box refinement are one kernel
         (ko_select_queries). Returns (ref [B, 300, 4], scores [B, 1600] or None, idx [B, 300])."""
-        om = memory * self.valid
-        _, om = self.enc_output.ln(om, self.enc_norm)
+        _, om = self.enc_output.ln(memory, self.enc_norm)
+        if self.enc_zero_row is not None:                   # masked proposals: the head's output for a zero row
+            om[:, self.masked] = self.enc_zero_row
         logits = self.enc_class(om)                                                             # [B, 1600, 11]
         delta = self._mlp3(om, self.enc_bbox)                                                   # [B, 1600, 4]
         ref, idx = K.select_queries(logits.contiguous(), delta.contiguous(), self.props, self.rp_xy, self.rp_ewh,
@@ -263,24 +285,34 @@ class RFDETR:
 
     # ---- decoder ----------------------------------------------------------------------------------------------
     def sine_embed(self, ref):
-        outs = []
-        for c in (1, 0, 2, 3):  # y, x, w, h
-            v = (ref[..., c] * (2 * math.pi))[..., None] / self.dim_t
-            outs.append(torch.stack([torch.sin(v[..., 0::2]), torch.cos(v[..., 1::2])], -1).reshape(*v.shape[:2], 128))
-        return torch.cat(outs, -1)
+        """model.py:188-194 in one kernel: [B, 300, 4] boxes -> [B, 300, 512]."""
+        return K.sine_embed(ref.contiguous(), self.dim_t)
+
+    def _query_feat(self, b: int) -> torch.Tensor:
+        """query_feat broadcast over the batch: a constant, made once per batch size outside graph capture (the
+        layers never write it) and made afresh inside a capture that meets a new size."""
+        t = self._tgt0.get(b)
+        if t is None:
+            t = self.query_feat.expand(b, N_QUERIES, D_MODEL).contiguous()
+            if not (t.is_cuda and torch.cuda.is_current_stream_capturing()):
+                self._tgt0[b] = t
+        return t
 
     def decoder(self, memory, ref):
         b = memory.shape[0]
         qpos = self.rph[1](self.rph[0](self.sine_embed(ref), "relu"))
-        tgt = self.query_feat.expand(b, N_QUERIES, D_MODEL).contiguous()
+        qp = self.pos_proj(qpos).reshape(b * N_QUERIES, -1)                    # qpos @ W of every layer
+        tgt = self._query_feat(b)
         values = self.vproj(memory)                                                              # [B, 1600, 1024]
         hd = D_MODEL // SA_HEADS
         for i, lyr in enumerate(self.dec):
-            qk = lyr["qk"](tgt + qpos).reshape(b, N_QUERIES, 2 * D_MODEL)                      # q | k columns
-            v = lyr["v"](tgt).reshape(b, N_QUERIES, D_MODEL)
-            o = K.attention(qk[..., :D_MODEL], qk[..., D_MODEL:], v, SA_HEADS, 1 / math.sqrt(hd))
+            c0 = i * self.pos_cols
+            # (tgt + qpos) @ [Wq | Wk] and tgt @ Wv in one GEMM: q | k | v columns
+            qkv = lyr["qkv"](tgt, addend=qp[:, c0:c0 + 2 * D_MODEL]).reshape(b, N_QUERIES, 3 * D_MODEL)
+            o = K.attention(qkv[..., :D_MODEL], qkv[..., D_MODEL:2 * D_MODEL], qkv[..., 2 * D_MODEL:], SA_HEADS,
+                            1 / math.sqrt(hd))
             _, tgt = lyr["out"].ln(o, lyr["norm1"], resid=tgt, write_h=False)                  # LN(tgt + out(o))
-            oa = lyr["offaw"](tgt + qpos)                                                         # [B, 300, 96]
+            oa = lyr["offaw"](tgt, addend=qp[:, c0 + 2 * D_MODEL:c0 + self.pos_cols])          # [B, 300, 96]
             loc, aw = K.deform_prep(oa, ref.contiguous(), CA_HEADS, CA_POINTS)  # locations + point softmax
             s = K.deform_attn(values, loc, aw, (GRID, GRID), CA_HEADS, D_MODEL // CA_HEADS, offset=i * D_MODEL)
             _, tgt = lyr["oproj"].ln(s, lyr["norm2"], resid=tgt, write_h=False)
@@ -301,8 +333,9 @@ class RFDETR:
         ref, _, _ = self.select_queries(memory, with_scores=False)
         hs = self.decoder(memory, ref)
         logits = self.class_embed(hs)
-        delta = self._mlp3(hs, self.bbox_embed)
-        boxes = torch.cat([delta[..., :2] * ref[..., 2:] + ref[..., :2], torch.exp(delta[..., 2:]) * ref[..., 2:]], -1)
+        h2 = self.bbox_embed[1](self.bbox_embed[0](hs, "relu"), "relu")
+        last = self.bbox_embed[2]                                 # the last box layer + the box refinement
+        boxes = K.box_head(h2, last.w, last.b, ref.contiguous())
         return boxes, logits
 
     __call__ = forward

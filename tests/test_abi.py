@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version_and_error_string():
-    assert _lib.lib().ko_abi_version() == 1
+    assert _lib.lib().ko_abi_version() == 2
     assert isinstance(_lib.lib().ko_last_error_string(), bytes)
 
 
@@ -44,11 +44,21 @@ def test_abi_version_and_error_string():
     ("ko_pack_weight_tf32x3", (16, 0, 8, 16, None)),                                        # K = 0
     ("ko_linear_gelu_f32_noalloc", (16, 16, None, 8, 1 << 20, 1 << 20, 16, None, None)),    # K*N over the scratch
     ("ko_linear_residual_ln_f32_packed",
-     (16, 16, None, None, None, 16, 16, 1e-6, 128, 256, 256, 99, None, 16, None, None)),    # unknown act
+     (16, 16, None, None, None, 16, 16, 1e-6, 128, 256, 256, 99, None, 16, 0, None, None)),  # unknown act
     ("ko_linear_residual_ln_f32_packed",
-     (16, 16, None, None, None, None, None, 1e-6, 128, 256, 256, 0, None, 16, None, None)), # no gamma / beta
-    ("ko_conv3x3_ln_f32_packed", (16, 16, 16, 16, 16, 1e-6, 1, 8, 8, 8, 256, 0, 32, None, None)),   # C % 16 != 0
-    ("ko_conv3x3_ln_f32_packed", (16, 16, 16, 16, 16, 1e-6, 1, 8, 8, 16, 256, 0, 16, None, None)),  # y aliases x
+     (16, 16, None, None, None, None, None, 1e-6, 128, 256, 256, 0, None, 16, 0, None, None)),  # no gamma/beta
+    ("ko_linear_residual_ln_f32_packed",
+     (16, 16, None, None, None, 16, 16, 1e-6, 128, 256, 256, 0, None, 32, 250, None, None)),  # ldy < N
+    ("ko_conv3x3_ln_f32_packed", (16, 0, 16, 16, 16, 16, 1e-6, 1, 8, 8, 8, 256, 0, 32, 0, None, None)),  # C % 16
+    ("ko_conv3x3_ln_f32_packed", (16, 0, 16, 16, 16, 16, 1e-6, 1, 8, 8, 16, 256, 0, 16, 0, None, None)),  # y is x
+    ("ko_conv3x3_ln_f32_packed", (16, 18, 16, 16, 16, 16, 1e-6, 1, 8, 8, 16, 256, 0, 32, 0, None, None)),  # ldx
+    ("ko_linear_add_f32_packed", (16, 16, None, 16, 512, 6, 8, 8, 8, 0, 32, None, None)),    # add_cols % 4
+    ("ko_linear_add_f32_packed", (16, 16, None, 20, 512, 8, 8, 8, 8, 0, 32, None, None)),    # addend unaligned
+    ("ko_linear_add_f32_packed", (16, 16, None, 16, 8, 12, 8, 8, 8, 0, 32, None, None)),     # add_cols > N
+    ("ko_linear_small_f32", (16, 16, None, 8, 256, 40, 0, 16, None)),                         # N > 32
+    ("ko_linear_small_f32", (16, 16, None, 8, 256, 11, 1, 16, None)),                         # GELU not offered
+    ("ko_box_head_f32", (16, 16, None, 20, 8, 256, 16, None)),                                # ref unaligned
+    ("ko_sine_embed", (16, 16, 10, 20, None)),                                                # out unaligned
     ("ko_attention_f32", (16, 16, 16, 16, 1, 128, 1, 48, 0, 48, 0, 48, 0, 48, 0, 48, 0.125, None, None)),  # HD 48
     ("ko_attention_f32", (16, 16, 16, 16, 1, 128, 1, 32, 0, 30, 0, 32, 0, 32, 0, 32, 0.125, None, None)),  # stride
     ("ko_layernorm", (16, 16, 16, 1e-6, 10, 6, 0, 16, None)),                                # C % 4 != 0
@@ -93,8 +103,11 @@ def test_linear_workspace_size():
     ("ko_linear_f32_packed", (16, 16, None, 256, 384, 1536, 0, 16, None, None)),
     ("ko_linear_gelu_f32", (16, 16, 16, 256, 384, 1536, 16, 16, 2 * 384 * 1536 * 4, None, None)),
     ("ko_linear_residual_ln_f32_packed",
-     (16, 16, None, None, None, 16, 16, 1e-6, 512, 384, 256, 0, None, 32, None, None)),
-    ("ko_conv3x3_ln_f32_packed", (16, 16, 16, 16, 16, 1e-6, 1, 8, 8, 16, 256, 0, 32, None, None)),
+     (16, 16, None, None, None, 16, 16, 1e-6, 512, 384, 256, 0, None, 32, 0, None, None)),
+    ("ko_conv3x3_ln_f32_packed", (16, 0, 16, 16, 16, 16, 1e-6, 1, 8, 8, 16, 256, 0, 32, 0, None, None)),
+    ("ko_linear_add_f32_packed", (16, 16, None, 32, 512, 256, 256, 384, 768, 0, 48, None, None)),
+    ("ko_linear_small_f32", (16, 16, None, 300, 256, 11, 0, 32, None)),
+    ("ko_box_head_f32", (16, 16, None, 32, 300, 256, 48, None)),
     ("ko_attention_f32", (16, 16, 16, 32, 1, 128, 1, 64, 0, 64, 0, 64, 0, 64, 0, 64, 0.125, None, None)),
     ("ko_im2col3x3", (16, 1, 8, 8, 8, 32, None)),
 ])

@@ -111,7 +111,7 @@ def test_rejects_unsupported_width(cuda):
     y = torch.empty((64, 320), device=cuda)
     with pytest.raises(_lib.KernelError):
         _lib.call("ko_linear_residual_ln_f32_packed", t(d["x"]).data_ptr(), pw.packed.data_ptr(), None, None, None,
-                  t(d["gamma"]).data_ptr(), t(d["beta"]).data_ptr(), 1e-6, 64, 64, 320, 0, None, y.data_ptr(),
+                  t(d["gamma"]).data_ptr(), t(d["beta"]).data_ptr(), 1e-6, 64, 64, 320, 0, None, y.data_ptr(), 0,
                   None, torch.cuda.current_stream().cuda_stream)
 
 

@@ -59,7 +59,35 @@ def _lrln(x, pw, gamma, beta, eps, resid=None, scale=None, act=None, h_out=None,
     o = _linear(x, pw)
     ho = (0 if resid is None else resid) + o * (1 if scale is None else scale)
     yy = F.layer_norm(ho, (ho.shape[-1],), gamma, beta, eps)
-    return (ho if write_h else None), (F.silu(yy) if act == "silu" else yy)
+    yy = F.silu(yy) if act == "silu" else yy
+    if y is not None:                     # written into the caller's buffer (possibly a channel slice)
+        y.copy_(yy.reshape(y.shape))
+        yy = y
+    return (ho if write_h else None), yy
+
+
+def _linear_add(x, pw, addend, act=None, out=None):
+    y = x @ pw.w + (0 if pw.b is None else pw.b)
+    y = y.reshape(-1, pw.n)
+    y = torch.cat([y[:, :addend.shape[1]] + addend, y[:, addend.shape[1]:]], 1)
+    return _linear(y.reshape(*x.shape[:-1], pw.n), _Packed(torch.eye(pw.n, dtype=y.dtype)), act)
+
+
+def _sine_embed(ref, dim_t, out=None):
+    outs = []
+    for c in (1, 0, 2, 3):
+        v = (ref[..., c] * (2 * math.pi))[..., None] / dim_t
+        outs.append(torch.stack([torch.sin(v[..., 0::2]), torch.cos(v[..., 1::2])], -1).reshape(*v.shape[:-1], 128))
+    return torch.cat(outs, -1)
+
+
+def _linear_small(x, w, bias=None, act=None):
+    return _linear(x, _Packed(w, bias), act)
+
+
+def _box_head(x, w, bias, ref):
+    d = x @ w + bias
+    return torch.cat([d[..., :2] * ref[..., 2:] + ref[..., :2], torch.exp(d[..., 2:]) * ref[..., 2:]], -1)
 
 
 def _select(logits, delta, prop, rp_xy, rp_ewh, nq, ref=None, idx=None):
@@ -71,7 +99,7 @@ def _select(logits, delta, prop, rp_xy, rp_ewh, nq, ref=None, idx=None):
 
 
 def _conv3x3_ln(x, pw, gamma, beta, eps, act=None, out=None):
-    return _lrln(_im2col3x3(x), pw, gamma, beta, eps, act=act, write_h=False)[1]
+    return _lrln(_im2col3x3(x), pw, gamma, beta, eps, act=act, y=out, write_h=False)[1]
 
 
 def _window_merge(h, grid_hw, win, out, col_off, gamma=None, beta=None, eps=1e-6, normalize=True):
@@ -124,6 +152,10 @@ def cpu_model(monkeypatch):
     monkeypatch.setattr(K, "window_merge_layernorm", _window_merge)
     monkeypatch.setattr(K, "window_partition_layernorm", _window_partition)
     monkeypatch.setattr(K, "deform_prep", _deform_prep)
+    monkeypatch.setattr(K, "linear_add", _linear_add)
+    monkeypatch.setattr(K, "sine_embed", _sine_embed)
+    monkeypatch.setattr(K, "linear_small", _linear_small)
+    monkeypatch.setattr(K, "box_head", _box_head)
     monkeypatch.setattr(K, "status_word", lambda *a: None)
     w = random_weights(0)
 

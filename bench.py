@@ -299,7 +299,7 @@ def run_ours(args, rank: int, world: int):
     latency = {}
     for nb in (1, 3):
         r_nb = det._runner(nb)
-        items_nb = items[:nb]
+        items_nb = [items[i % B] for i in range(nb)]
         ts = []
         with torch.cuda.stream(stream):
             for it in range(25):

@@ -160,7 +160,7 @@ class RFDETR:
         self.masked = torch.nonzero(self.valid[:, 0] == 0)[:, 0]
         self.enc_zero_row = None
         if self.masked.numel():
-            _, self.enc_zero_row = self.enc_output.ln(torch.zeros((1, D_MODEL), device=dev), self.enc_norm)
+            _, self.enc_zero_row = self.enc_output.ln(torch.zeros((1, D_MODEL), device=self.device), self.enc_norm)
         self.props = p["proposals"]
         rp = p["refpoint_embed"]
         self.rp_xy, self.rp_ewh = rp[:, :2].contiguous(), torch.exp(rp[:, 2:]).contiguous()

@@ -20,12 +20,6 @@
 // and the softmax over each head's points (model.py:222-225), one thread per (frame, query, head).
 #include "ko_common.cuh"
 
-// Frames ahead whose value map a CTA streams into L2 before sampling its own (-1: none). Measurement builds may
-// override it (-DKO_DEFORM_PF_AHEAD=n).
-#ifndef KO_DEFORM_PF_AHEAD
-#define KO_DEFORM_PF_AHEAD -1
-#endif
-
 namespace {
 
 struct DeformShape {
@@ -90,25 +84,8 @@ __global__ void __launch_bounds__(256) deform_vec4_kernel(const float* __restric
 __global__ void __launch_bounds__(256) deform_vec4_np2_kernel(const float* __restrict__ value,
                                                               const float* __restrict__ loc,
                                                               const float* __restrict__ aw, DeformShape s,
-                                                              float* __restrict__ out, int pf_ahead) {
+                                                              float* __restrict__ out) {
   const int64_t groups = s.HD >> 2;
-  if (pf_ahead >= 0) {
-    // Stream this CTA's share of the value map of frame (own frame + pf_ahead) into L2 in row order, so the
-    // CTAs that sample that frame later gather from L2 instead of making random DRAM accesses.
-    const int64_t tpf = s.NQ * s.NH * groups;  // threads per frame
-    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x;
-    const int64_t b0 = t0 / tpf, pb = b0 + pf_ahead;
-    if (pb < s.B) {
-      const int64_t rows = s.GH * s.GW, o = t0 - b0 * tpf;
-      const int64_t r0 = o * rows / tpf, r1 = min(rows, (o + blockDim.x) * rows / tpf);
-      const int64_t r = r0 + threadIdx.x;
-      if (r < r1) {
-        const float* p = value + (pb * rows + r) * s.ROW + s.offset;
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(static_cast<uint32_t>(s.NH * s.HD * 4))
-                     : "memory");
-      }
-    }
-  }
   const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t total = s.B * s.NQ * s.NH * groups;
   if (t >= total) return;
@@ -213,7 +190,7 @@ extern "C" int ko_deform_attn(const float* value, const float* loc, const float*
   const bool np2 = vec && NP == 2 && (reinterpret_cast<uintptr_t>(loc) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(aw) & 7) == 0;
   if (np2)
-    deform_vec4_np2_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(value, loc, aw, s, out, KO_DEFORM_PF_AHEAD);
+    deform_vec4_np2_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(value, loc, aw, s, out);
   else if (vec)
     deform_vec4_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(value, loc, aw, s, out);
   else

@@ -131,10 +131,10 @@ def instrumented_step(det, runner_x, items, K):
 
     timers = {n: EventTimer() for n in ("gemm_tf32x3", "gemm_residual_ln", "attention_tf32x3", "residual_layernorm",
                                          "deform_attn", "preprocess")}
-    orig = {n: getattr(K, n) for n in ("linear", "linear_residual_layernorm", "attention", "residual_layernorm",
-                                       "deform_attn", "preprocess_batch")}
+    orig = {n: getattr(K, n) for n in ("linear", "linear_add", "linear_residual_layernorm", "attention",
+                                       "residual_layernorm", "deform_attn", "preprocess_batch")}
 
-    def gemm_work(x, pw, act=None, out=None):
+    def gemm_work(x, pw, *a, **k):
         return 2.0 * (x.numel() // pw.k) * pw.k * pw.n
 
     def gemm_ln_work(x, pw, *a, **k):
@@ -156,6 +156,7 @@ def instrumented_step(det, runner_x, items, K):
         return float(sum(img.numel() for img, *_ in items_) + len(items_) * dst * dst * 3 * 4)
 
     K.linear = timers["gemm_tf32x3"].wrap(orig["linear"], gemm_work)
+    K.linear_add = timers["gemm_tf32x3"].wrap(orig["linear_add"], gemm_work)   # the same kernel, + an addend
     K.linear_residual_layernorm = timers["gemm_residual_ln"].wrap(orig["linear_residual_layernorm"], gemm_ln_work)
     K.attention = timers["attention_tf32x3"].wrap(orig["attention"], attn_work)
     K.residual_layernorm = timers["residual_layernorm"].wrap(orig["residual_layernorm"], ln_work)

@@ -52,10 +52,7 @@ constexpr int kThreads = 13 * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;      // two S / P_hi buffers of 128 columns
 constexpr uint32_t kColPlo = 256;  // P_lo, 128 columns
-constexpr uint32_t kColO = 384;    // the O_j buffer, HD columns
-// Q_hi, HD columns after O: the A operand of two of the three S products comes from tensor memory
-template <int HD>
-constexpr uint32_t kColQ = kColO + HD;
+constexpr uint32_t kColO = 384;    // two O_j buffers of HD columns
 
 struct AttnArgs {
   const float* q;
@@ -72,16 +69,15 @@ struct AttnArgs {
 template <int HD>
 struct AttnCfg {
   static constexpr int kKB = HD / 32;                          // 128-byte k-blocks of a q / k row
-  static constexpr uint32_t kQBytes = BQ * HD * 4;             // Q_lo (the q tile lands here in fp32 first)
+  static constexpr uint32_t kQBytes = BQ * HD * 4;             // one of Q_hi / Q_lo
   static constexpr uint32_t kKBytes = BKEY * HD * 4;           // one of K_hi / K_lo
   static constexpr uint32_t kVBytes = HD * BKEY * 4;           // one of Vt_hi / Vt_lo
-  static constexpr uint32_t kOffQlo = 0;
-  static constexpr uint32_t kOffKhi = kQBytes;
+  static constexpr uint32_t kOffQlo = kQBytes;
+  static constexpr uint32_t kOffKhi = 2 * kQBytes;
   static constexpr uint32_t kOffKlo = kOffKhi + kKBytes;
-  static constexpr uint32_t kOffV = kOffKlo + kKBytes;         // two v buffers, each Vt_hi then Vt_lo
-  static constexpr uint32_t kVBufBytes = 2 * kVBytes;
-  static constexpr uint32_t kOffBars = kOffV + 2 * kVBufBytes;
-  static_assert(kColQ<HD> + HD <= kTmemCols, "TMEM columns");
+  static constexpr uint32_t kOffVhi = kOffKlo + kKBytes;
+  static constexpr uint32_t kOffVlo = kOffVhi + kVBytes;
+  static constexpr uint32_t kOffBars = kOffVlo + kVBytes;
   // At least 120 KB even where the tiles need less (head dim 32), so that one CTA per SM holds all 512 tensor-
   // memory columns and no second CTA waits in tcgen05.alloc.
   static constexpr size_t kSmemNeed = 1024 + kOffBars + 256;
@@ -164,14 +160,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
-  uint64_t* q_ready = bars + 0;   // Q_lo in place, Q_hi in TMEM (4 v-loader warps)
+  uint64_t* q_ready = bars + 0;   // q tile split            (4 v-loader warps)
   uint64_t* k_full = bars + 1;    // k tile written          (4 k-loader warps)
-  uint64_t* v_full = bars + 2;    // v buffer written, x2    (4 v-loader warps)
-  uint64_t* v_empty = bars + 4;   // v buffer read, x2       (1 commit)
-  uint64_t* s_full = bars + 6;    // S_j complete, x2        (1 commit)
-  uint64_t* p_full = bars + 8;    // P_j written             (4 softmax warps)
-  uint64_t* o_full = bars + 9;    // O_j complete            (1 commit)
-  uint64_t* o_empty = bars + 10;  // O_j consumed            (4 softmax warps)
+  uint64_t* v_full = bars + 3;    // v tile written          (4 v-loader warps)
+  uint64_t* s_full = bars + 5;    // S_j complete, x2        (1 commit)
+  uint64_t* p_full = bars + 7;    // P_j written             (4 softmax warps)
+  uint64_t* o_full = bars + 8;    // O_j complete, x2        (1 commit)
+  uint64_t* o_empty = bars + 10;  // O_j consumed, x2        (4 softmax warps)
   uint64_t* mma_done = bars + 12;
   uint64_t* plo_free = bars + 13;  // P_j.V_j's P_lo products done (1 commit)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
@@ -186,13 +181,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
   if (threadIdx.x == 0) {
     mbar_init(q_ready, 4);
     mbar_init(k_full, 4);
+    mbar_init(v_full, 4);
     mbar_init(p_full, 4);
-    mbar_init(o_full, 1);
-    mbar_init(o_empty, 4);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&v_full[i], 4);
-      mbar_init(&v_empty[i], 1);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 4);
     }
     mbar_init(mma_done, 1);
     mbar_init(plo_free, 1);
@@ -223,19 +217,16 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
   if (warp == 0) {
     // ---------------- MMA issuer ----------------
     // Order on the tensor pipe: S_0, then per block j: S_{j+1} (into the other S buffer, overlapping softmax_j),
-    // P_j.V_j. S_{j+1} reuses the buffer of P_{j-1}, so it waits for P_{j-1}.V_{j-1} to complete. P_j.V_j reads
-    // v buffer j & 1 and overwrites O, so it waits for the softmax warps to have folded O_{j-1} into their rows.
+    // P_j.V_j. S_{j+1} reuses the buffer of P_{j-1}, so it waits for P_{j-1}.V_{j-1} to complete.
     // The whole warp runs this loop with the same values in every lane; one elected lane issues each MMA.
     {
       // Descriptors are built once; an MMA's operand is its tile's descriptor plus the byte offset / 16 (the
       // start-address field; shared addresses stay below 2^18 bytes, so the field cannot overflow).
       const uint32_t sb = smem_addr(smem);
       constexpr uint32_t idesc_o = idesc_tf32(BQ, HD);
-      const uint64_t dq_lo = smem_desc_k_sw128(sb + C::kOffQlo);
-      const uint32_t tq_hi = tmem + kColQ<HD>;  // Q_hi: 128 lanes x HD columns, one element per column
+      const uint64_t dq_hi = smem_desc_k_sw128(sb), dq_lo = smem_desc_k_sw128(sb + C::kOffQlo);
       const uint64_t dk_hi = smem_desc_k_sw128(sb + C::kOffKhi), dk_lo = smem_desc_k_sw128(sb + C::kOffKlo);
-      const uint64_t dv0 = smem_desc_k_sw128(sb + C::kOffV), dv1 = smem_desc_k_sw128(sb + C::kOffV + C::kVBufBytes);
-      constexpr uint64_t kVloOff = C::kVBytes >> 4;  // Vt_lo follows Vt_hi in each v buffer
+      const uint64_t dv_hi = smem_desc_k_sw128(sb + C::kOffVhi), dv_lo = smem_desc_k_sw128(sb + C::kOffVlo);
       // A short last key block (e.g. 17 of the 401 keys of a window) gets MMAs only as wide / deep as its keys:
       // N = keys rounded up to 16 for S, K = keys rounded up to 8 for P.V.
       auto keys_of = [&](int j) { return min(BKEY, a.L - j * BKEY); };
@@ -245,9 +236,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
 #pragma unroll
         for (int s = 0; s < C::kKB * 4; ++s) {  // 8-wide k-steps over the head dimension
           const uint64_t off = static_cast<uint64_t>(((s >> 2) * (BQ * 128) + (s & 3) * 32) >> 4);
-          mma_tf32_w(d, dq_lo + off, dk_hi + off, idesc_s, s == 0 ? 0u : 1u);  // Q_lo from shared memory
-          mma_tf32_ts_w(d, tq_hi + 8 * s, dk_lo + off, idesc_s, 1u);            // Q_hi from tensor memory
-          mma_tf32_ts_w(d, tq_hi + 8 * s, dk_hi + off, idesc_s, 1u);
+          mma_tf32_w(d, dq_lo + off, dk_hi + off, idesc_s, s == 0 ? 0u : 1u);
+          mma_tf32_w(d, dq_hi + off, dk_lo + off, idesc_s, 1u);
+          mma_tf32_w(d, dq_hi + off, dk_hi + off, idesc_s, 1u);
         }
         mma_commit_w(&s_full[j & 1]);  // the k loaders wait on it too (S_j done = k tile j free)
       };
@@ -259,19 +250,18 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
       for (int j = 0; j < nkb && ok; ++j) {
         if (j + 1 < nkb) {
           if (!warp_wait(k_full, static_cast<uint32_t>(j + 1) & 1u, abort_flag)) break;
-          if (j >= 1 && !warp_wait(o_full, static_cast<uint32_t>(j - 1) & 1u, abort_flag)) break;
+          if (j >= 1 && !warp_wait(&o_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag)) break;
           tc_fence_after();
           issue_s(j + 1);
         }
-        // O_j = P_j V_j, once P_j is written, v tile j landed in buffer j & 1 and O_{j-1} was consumed
+        // O_j = P_j V_j into O buffer j & 1, once P_j is written, V_j landed and the buffer was consumed
         if (!warp_wait(p_full, static_cast<uint32_t>(j) & 1u, abort_flag) ||
-            !warp_wait(&v_full[j & 1], static_cast<uint32_t>(j >> 1) & 1u, abort_flag) ||
-            (j >= 1 && !warp_wait(o_empty, static_cast<uint32_t>(j - 1) & 1u, abort_flag)))
+            !warp_wait(v_full, static_cast<uint32_t>(j) & 1u, abort_flag) ||
+            !warp_wait(&o_empty[j & 1], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, abort_flag))
           break;
         tc_fence_after();
-        const uint32_t d = tmem + kColO;
+        const uint32_t d = tmem + kColO + static_cast<uint32_t>(j & 1) * HD;
         const uint32_t p_hi = tmem + kColS + static_cast<uint32_t>(j & 1) * BKEY;
-        const uint64_t dv_hi = (j & 1) ? dv1 : dv0, dv_lo = dv_hi + kVloOff;
         const int ksteps = (keys_of(j) + 7) >> 3;
         // The P_lo products first, then a commit that hands the P_lo columns back to the softmax warps: they
         // write P_{j+1} while the P_hi products of this block (two thirds of its MMAs) still run. A full block's
@@ -304,9 +294,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
             mma_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + off, idesc_o, 1u);
           }
         }
-        // P_j.V_j done: v buffer j & 1 is free for tile j + 2, and O_j is ready for the softmax warps.
-        mma_commit_w(&v_empty[j & 1]);
-        mma_commit_w(o_full);
+        // One commit per event: the v loaders wait on o_full as well (P_j.V_j done = v tile j free).
+        mma_commit_w(&o_full[j & 1]);
       }
       // Drain: every MMA this warp issued completes before tensor memory is released.
       mma_commit_w(mma_done);
@@ -329,9 +318,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
     float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
     bool ok = true;
     auto add_block = [&](int jb, float alpha) -> bool {  // o = o * alpha + O_jb
-      if (!warp_wait(o_full, static_cast<uint32_t>(jb) & 1u, abort_flag)) return false;
+      if (!warp_wait(&o_full[jb & 1], static_cast<uint32_t>(jb >> 1) & 1u, abort_flag)) return false;
       tc_fence_after();
-      const uint32_t ob = trow + kColO;
+      const uint32_t ob = trow + kColO + static_cast<uint32_t>(jb & 1) * HD;
 #pragma unroll
       for (int c = 0; c < HD / 16; ++c) {
         uint32_t r[16];
@@ -342,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(o_empty);
+      if (lane == 0) mbar_arrive(&o_empty[jb & 1]);
       return true;
     };
     for (int j = 0; j < nkb; ++j) {
@@ -449,38 +438,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
     constexpr int kGroup = kLoadThreads / 2;       // 128 threads per group
     constexpr int kTileChunks = BKEY * HD / 4 / kGroup;
     const int g = t & (kGroup - 1);
-    // q: each warp of the v group takes the 32 rows of its tensor-memory lane quadrant (warps 9-12 cover the four
-    // quadrants); a thread splits its row of the fp32 tile that TMA brought in, leaves Q_lo in place in shared
-    // memory and writes Q_hi into the row's lane of tensor memory.
     auto write_q = [&]() -> bool {
       if (!mbar_wait(q_tma, 0, abort_flag)) return false;
-      const int quad = warp & 3, r = quad * 32 + lane;
-      const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16) + kColQ<HD>;
-#pragma unroll
-      for (int ci = 0; ci < HD / 16; ++ci) {  // 16 columns = four 16-byte chunks of one 128-byte k-block row
-        uint32_t hv[16];
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int d = 16 * ci + 4 * cc, kb = d >> 5, c = (d & 31) >> 2;
-          float4* p = reinterpret_cast<float4*>(smem + C::kOffQlo + kb * (BQ * 128) + sw128(r, c));
-          const float4 v = *p;
-          float4 hi, lo;
-          split_tf32(v.x, hi.x, lo.x);
-          split_tf32(v.y, hi.y, lo.y);
-          split_tf32(v.z, hi.z, lo.z);
-          split_tf32(v.w, hi.w, lo.w);
-          *p = lo;
-          hv[4 * cc + 0] = __float_as_uint(hi.x);
-          hv[4 * cc + 1] = __float_as_uint(hi.y);
-          hv[4 * cc + 2] = __float_as_uint(hi.z);
-          hv[4 * cc + 3] = __float_as_uint(hi.w);
-        }
-        tmem_st_32x32b_x16(tq + 16 * ci, hv);
-      }
-      tmem_st_wait();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
+      split_in_place(0, C::kOffQlo, static_cast<int>(C::kQBytes / 16), g, kGroup);
       if (lane == 0) mbar_arrive(q_ready);
       return true;
     };
@@ -539,11 +499,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
       const bool vok = write_q();
       load(0);
       for (int j = 0; j < nkb && vok; ++j) {
-        // v tile j goes into buffer j & 1 over tile j-2: P_{j-2}.V_{j-2} must be complete
-        const int vb = j & 1;
-        if (j >= 2 && !mbar_wait(&v_empty[vb], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag)) break;
-        uint8_t* vhi = smem + C::kOffV + vb * C::kVBufBytes;
-        uint8_t* vlo = vhi + C::kVBytes;
+        // v tile j overwrites tile j-1: P_{j-1}.V_{j-1} must be complete
+        if (j >= 1 && !mbar_wait(&o_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag)) break;
 #pragma unroll
         for (int i = 0; i < kTileChunks; ++i) {
           const int idx = i * kGroup + g, key = idx & (BKEY - 1), dq = idx / BKEY;
@@ -554,13 +511,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
             const int d = 4 * dq + e;
             const uint32_t off = base + sw128(d, (key & 31) >> 2);
             const float hi = src[e], lo = tf32_tail(src[e]);  // v itself as hi: P.V errors are not amplified
-            *reinterpret_cast<float*>(vhi + off) = hi;
-            *reinterpret_cast<float*>(vlo + off) = lo;
+            *reinterpret_cast<float*>(smem + C::kOffVhi + off) = hi;
+            *reinterpret_cast<float*>(smem + C::kOffVlo + off) = lo;
           }
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&v_full[vb]);
+        if (lane == 0) mbar_arrive(v_full);
         if (j + 1 < nkb) load(j + 1);
       }
     }

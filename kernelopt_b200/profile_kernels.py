@@ -18,6 +18,10 @@ Kernels and workloads (per frame of batch B; the algorithmic traffic or flops co
               W [384, 384]; flops = 2*M*384*384 (outproj_unfused: the GEMM, then the residual + LN kernel)
   fc2_ln      the same for fc2: x [B*1604, 1536], W [1536, 384] (fc2_unfused likewise)
   qkv         the fused QKV projection: x [B*1604, 384] @ W [384, 1152] + b; flops = 2*M*384*1152
+  conv3x3_ln  the projector's bottleneck conv: x NHWC [B, 40, 40, 128], 3x3 -> 128 channels, LayerNorm + SiLU
+              (implicit GEMM); flops = 2*M*1152*128
+  cv1_ln      the projector's first 1x1 conv: x [B*1600, 1536] -> 256 channels, LayerNorm + SiLU; flops =
+              2*M*1536*256
 Each timed iteration is preceded, outside the events, by a write and a read-back of a 256 MB buffer (larger
 than the 126 MB L2): every launch starts with a cold L2 that holds no dirty lines of the flush (their write-back
 would otherwise be charged to the timed kernel), and a short spin kernel holds the stream while the host enqueues the
@@ -84,6 +88,19 @@ def setup(kernel: str, b: int, dev, policy: str = "reference"):
             pw = K.pack_weight(w)
             fn = lambda: K.residual_layernorm(h, K.linear(x, pw), bias, scale, gamma, beta, 1e-6)  # noqa: E731
         return fn, 2.0 * m * k * 384, "flop"
+    if kernel in ("conv3x3_ln", "cv1_ln"):
+        cin, cout, k = (128, 128, 9 * 128) if kernel == "conv3x3_ln" else (1536, 256, 1536)
+        x = torch.randn(b, 40, 40, cin, generator=g).to(dev)
+        w = (torch.randn(k, cout, generator=g) / k ** 0.5).to(dev)
+        gamma = (1 + 0.1 * torch.randn(cout, generator=g)).to(dev)
+        beta = (0.1 * torch.randn(cout, generator=g)).to(dev)
+        pw = K.pack_weight(w)
+        if kernel == "conv3x3_ln":
+            fn = lambda: K.conv3x3_layernorm(x, pw, gamma, beta, 1e-6, "silu")  # noqa: E731
+        else:
+            fn = lambda: K.linear_residual_layernorm(x.reshape(-1, cin), pw, gamma, beta, 1e-6, act="silu",  # noqa: E731
+                                                     write_h=False)
+        return fn, 2.0 * b * 1600 * k * cout, "flop"
     if kernel == "qkv":
         m = b * 1604
         a = torch.randn(m, 384, generator=g).to(dev)
@@ -113,7 +130,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True, choices=["preprocess", "preprocess_1080p", "resln", "gemm", "deform", "deform_model",
                                                              "attn", "attn_win",
-                                                             "outproj_ln", "outproj_unfused", "fc2_ln", "fc2_unfused", "qkv"])
+                                                             "outproj_ln", "outproj_unfused", "fc2_ln", "fc2_unfused", "qkv",
+                                                             "conv3x3_ln", "cv1_ln"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)

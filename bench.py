@@ -38,13 +38,15 @@ WORKLOAD = ("RF-DETR-Medium fp32 inference on seeded 1920x1080 uint8 BGR frames:
             "projector + top-300 selection + 4-layer deformable decoder + heads, random-init weights (seed 0)")
 
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per plain GEMM launch (gemm_tf32x3_kernel with the
-# bias / activation epilogue), mean over the 50 such launches of one step at 64 frames, from one ncu capture:
-#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --cache-control none
-#       --clock-control none -k regex:gemm_tf32x3 -c 95 python bench.py --steps 1 --warmup 3 --no-cpu-baseline
-# (the first 95 launches matching the pattern are one forward's 50 plain and 45 LayerNorm-epilogue GEMMs; the plain
-# ones total 19 125 MB against 20 089 MB of algorithmic bytes: x, the output and the split weight once each).
-GEMM_TRAFFIC_PER_LAUNCH = {64: 382.5e6}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per plain GEMM launch, mean over the 45 plain GEMM
+# launches of one 64-frame forward: their algorithmic bytes (x, output, split weight, addend; 450.7 MB per launch)
+# times the traffic/algorithmic ratio that one-launch captures of the two largest shapes measured (0.836), each
+# from a 32-frame case of one kernel:
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --clock-control none
+#       -k regex:gemm_tf32x3 -s 1 -c 1 python -m kernelopt_b200.profile_kernels --kernel gemm --batch 32 \
+#       --iters 1 --warmup 1                                    (and --kernel qkv)
+# (table and derivation: profiles/gemm_tf32x3_traffic_per_shape.md).
+GEMM_TRAFFIC_PER_LAUNCH = {64: 376.8e6}
 
 
 def frames_for(rank: int, n: int) -> np.ndarray:
@@ -335,7 +337,8 @@ def run_ours(args, rank: int, world: int):
     dk = kernels[dom]
     roofline = {"kernel": dom, "bound": dk["bound"], "achieved": dk["achieved"], "peak": dk["peak"],
                 "unit": dk["unit"], "frac": dk["frac"], "traffic": GEMM_TRAFFIC_PER_LAUNCH.get(B) if dom == "gemm_tf32x3"
-                else None, "traffic_unit": "bytes per launch (ncu dram read + write, mean over the step's launches)",
+                else None, "traffic_unit": "bytes per launch (ncu dram read + write, per-shape one-launch captures scaled to "
+                "the step's plain GEMM launches)",
                 "peak_source": ("3xTF32 ceiling = measured bf16 dense / 6 (" + peaks["source"] + ")"
                                 if dk["bound"] == "tensor" else f"{peaks['source']} HBM copy bandwidth"),
                 "step_share_eager": dk["ms_per_step"] / (1e3 * secs / args.steps)}

@@ -13,6 +13,7 @@
 // launch. Three output layouts share the kernel: HWC (the reference's), CHW (NCHW batches) and PATCH16 (the
 // im2col of the ViT 16x16 patch embedding, which turns that convolution into a plain GEMM).
 #include <cstring>
+#include <type_traits>
 
 #include "ko_common.cuh"
 
@@ -132,7 +133,11 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(const __grid_const
 // overlap the arithmetic of this one. Per output element the loop does 4 byte loads from shared memory, the
 // integer tap arithmetic, one LUT load from shared memory and a quarter of a 128-bit store.
 // ---------------------------------------------------------------------------------------------------------
-constexpr int kBandThreads = 256;
+// Threads per band CTA; measurement builds may override it (-DKO_PRE_BAND_THREADS=n, a multiple of 32, <= 1024).
+#ifndef KO_PRE_BAND_THREADS
+#define KO_PRE_BAND_THREADS 256
+#endif
+constexpr int kBandThreads = KO_PRE_BAND_THREADS;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(kodev::smem_addr(smem)), "l"(gmem) : "memory");
@@ -173,7 +178,7 @@ __device__ __forceinline__ float4 item_values(const uint8_t* s0, const uint8_t* 
 }
 
 template <int IPT>
-__global__ void __launch_bounds__(kBandThreads) preprocess_band_kernel(const __grid_constant__ BatchParams p,
+__global__ void __launch_bounds__(kBandThreads, kBandThreads <= 256 ? 3 : 2) preprocess_band_kernel(const __grid_constant__ BatchParams p,
                                                                        const float* __restrict__ lut, int dst,
                                                                        int layout, float* __restrict__ out,
                                                                        int row_cap, int band) {
@@ -269,27 +274,42 @@ __global__ void __launch_bounds__(kBandThreads) preprocess_band_kernel(const __g
   }
 
   // Three row-pair buffers: the pair of row y+1 is staged into the buffer row y-2 used, which every thread has
-  // finished reading before it passed the barrier of row y-1; so one barrier per row suffices.
-  for (int y = y_begin, buf = 0; y < y_end; ++y, buf = buf == 2 ? 0 : buf + 1) {
-    const int4 yt = yt_next;
-    if (y + 1 < y_end) {
-      yt_next = stage(y + 1, buf == 2 ? 0 : buf + 1);
-    } else {
-      cp_async_commit();  // empty group keeps the wait count uniform
-    }
-    cp_async_wait_1();
-    __syncthreads();
-    const uint8_t* s0 = rowbuf + (2 * buf) * row_cap;
-    const uint8_t* s1 = s0 + row_cap;
-    const int64_t rt = row_term(layout, y, dst);
+  // finished reading before it passed the barrier of row y-1; so one barrier per row suffices. The loop is
+  // unrolled over the ring (the buffer of each step is a constant) and specialised for the table mode, which is
+  // the same for the whole CTA (one image).
+  auto rows = [&](auto mode_c) {
+    constexpr int MODE = decltype(mode_c)::value;
+    int y = y_begin;
+    auto step = [&](auto buf_c) -> bool {
+      constexpr int BUF = decltype(buf_c)::value;
+      if (y >= y_end) return false;
+      const int4 yt = yt_next;
+      if (y + 1 < y_end) {
+        yt_next = stage(y + 1, (BUF + 1) % 3);
+      } else {
+        cp_async_commit();  // empty group keeps the wait count uniform
+      }
+      cp_async_wait_1();
+      __syncthreads();
+      const uint8_t* s0 = rowbuf + (2 * BUF) * row_cap;
+      const uint8_t* s1 = s0 + row_cap;
+      const int64_t rt = row_term(layout, y, dst);
 #pragma unroll
-    for (int k = 0; k < IPT; ++k) {
-      if (!live[k]) continue;
-      const float4 v = mode == 0 ? item_values<0>(s0, s1, tap[k], chans[k], yt, slut)
-                                 : item_values<1>(s0, s1, tap[k], chans[k], yt, slut);
-      *reinterpret_cast<float4*>(obase[k] + rt) = v;
+      for (int k = 0; k < IPT; ++k) {
+        if (!live[k]) continue;
+        *reinterpret_cast<float4*>(obase[k] + rt) = item_values<MODE>(s0, s1, tap[k], chans[k], yt, slut);
+      }
+      ++y;
+      return true;
+    };
+    while (step(std::integral_constant<int, 0>{}) && step(std::integral_constant<int, 1>{}) &&
+           step(std::integral_constant<int, 2>{})) {
     }
-  }
+  };
+  if (mode == 0)
+    rows(std::integral_constant<int, 0>{});
+  else
+    rows(std::integral_constant<int, 1>{});
 }
 
 int validate_image(const ko_image_desc& d, int64_t dst, const char* who) {

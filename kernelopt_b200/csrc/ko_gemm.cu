@@ -43,24 +43,9 @@ namespace {
 using namespace kodev;
 
 constexpr int BM = 128;
-constexpr int kTransformWarp0 = 2;   // warps 2..: one or two groups of four split the k-blocks
-constexpr int EPI_ACT = 0;
-constexpr int EPI_LN = 1;
-
-// Warp roles per variant: warp 0 TMA, warp 1 MMA, then the split warps, then 8 epilogue warps (two per TMEM lane
-// quadrant). Two split groups take alternate k-blocks; the LayerNorm epilogue with the correction accumulator
-// (K > 512, where each k-block's MMAs take long enough for one group to keep up) uses one group, so the CTA has
-// 14 warps — at most four per SM sub-partition, which lets ptxas give each thread 128 registers instead of the
-// 96 of 18 warps (five on two of the sub-partitions), where that epilogue spilled.
-#ifndef KO_GEMM_ONE_GROUP_ALL_LN  // measurement builds: -DKO_GEMM_ONE_GROUP_ALL_LN=1 gives every LN variant one group
-#define KO_GEMM_ONE_GROUP_ALL_LN 0
-#endif
-template <int EPI, bool SPLIT>
-struct Roles {
-  static constexpr int kTransformGroups = (EPI == EPI_LN && (SPLIT || KO_GEMM_ONE_GROUP_ALL_LN)) ? 1 : 2;
-  static constexpr int kEpilogueWarp0 = kTransformWarp0 + 4 * kTransformGroups;
-  static constexpr int kThreads = (kEpilogueWarp0 + 8) * 32;
-};
+constexpr int kTransformWarp0 = 2;   // warps 2-9: two groups of four split alternate k-blocks
+constexpr int kEpilogueWarp0 = 10;   // warps 10-17: two warps per TMEM lane quadrant
+constexpr int kThreads = 18 * 32;
 constexpr uint32_t kStoreTileBytes = 32 * 32 * 4;                   // one epilogue warp's 32x32 output tile
 constexpr uint32_t kStoreBytes = 8 * kStoreTileBytes;               // 32 KB of staging for the TMA stores
 constexpr size_t kSmemBudget = 224 * 1024 - kStoreBytes;  // stage buffers; staging, barriers, slack on top
@@ -70,9 +55,10 @@ constexpr size_t kSmemBudget = 224 * 1024 - kStoreBytes;  // stage buffers; stag
 // accumulator in the epilogue. The tensor core's fp32 accumulation drops low-order bits at every MMA; with a
 // single accumulator the 2 x K/8 correction MMAs land on a large running sum, which makes the error grow with
 // K. With SPLIT they land on a small one, and the large sum sees only K/8 additions.
-// Epilogue kinds (EPI_ACT, EPI_LN above). EPI_ACT: out = act(acc + bias). EPI_LN: v = resid + (acc + bias) *
-// scale over whole rows (the N columns of a row are split over the CTAs of a cluster), y = act(LayerNorm(v) *
-// gamma + beta).
+// Epilogue kinds. EPI_ACT: out = act(acc + bias). EPI_LN: v = resid + (acc + bias) * scale over whole rows
+// (the N columns of a row are split over the CTAs of a cluster), y = act(LayerNorm(v) * gamma + beta).
+constexpr int EPI_ACT = 0;
+constexpr int EPI_LN = 1;
 
 // Row statistics exchange of the LayerNorm epilogue: per tile parity, the two epilogue warps of a lane
 // quadrant publish (mean, M2) of their half of the row [2][2][128] float2, and the cluster peer's CTA-level
@@ -231,15 +217,13 @@ __device__ __forceinline__ float ln_act(float r, int act) {
 }
 
 template <int BN, int BKB, bool SPLIT, int EPI>
-__global__ void __launch_bounds__(Roles<EPI, SPLIT>::kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_whi,
                        const __grid_constant__ CUtensorMap map_wlo, const __grid_constant__ CUtensorMap map_out,
                        const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_r,
                        const GemmArgs args) {
   using C = Cfg<BN, BKB, SPLIT, EPI>;
   constexpr int S = C::kStages;
-  constexpr int kEpilogueWarp0 = Roles<EPI, SPLIT>::kEpilogueWarp0;
-  constexpr uint32_t kGroups = Roles<EPI, SPLIT>::kTransformGroups;
   constexpr int NB = C::kAccBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -432,8 +416,8 @@ __global__ void __launch_bounds__(Roles<EPI, SPLIT>::kThreads, 1)
     }
   } else if (warp < kEpilogueWarp0) {
     // ---------------- x split: hi in place, lo alongside ----------------
-    // With two groups, group g (warps 2-5 or 6-9) takes the k-blocks whose running index has parity g, so two
-    // stages are split at once and each group has two MMA k-blocks of time per stage; one group takes them all.
+    // Group g (warps 2-5 or 6-9) takes the k-blocks whose running index has parity g, so two stages are
+    // split at once and each group has two MMA k-blocks of time per stage.
     const int group = (warp - kTransformWarp0) >> 2;
     const int t = (threadIdx.x - kTransformWarp0 * 32) & 127;  // 0..127 within the group
     constexpr int kPer = static_cast<int>(C::kATileBytes / 16 / 128);  // float4 of the tile per thread
@@ -456,7 +440,7 @@ __global__ void __launch_bounds__(Roles<EPI, SPLIT>::kThreads, 1)
         }
       }
       for (int kb = 0; kb < args.k_blocks; ++kb, ++it) {
-        if (it % kGroups == static_cast<uint32_t>(group)) {
+        if ((it & 1u) == static_cast<uint32_t>(group)) {
           if (!mbar_wait(&full[st], phase, abort_flag)) {
             ok = false;
             break;
@@ -901,8 +885,7 @@ int launch_gemm(const float* x, const float* w_packed, const float* bias, const 
   const int tiles = a.m_tiles * a.n_tiles;
   const int grid = std::min(tiles, info.sm_count);
   a.cs = 1;
-  gemm_tf32x3_kernel<BN, BKB, SPLIT, EPI_ACT><<<grid, Roles<EPI_ACT, SPLIT>::kThreads, C::kSmemBytes, stream>>>(
-      mx, mhi, mlo, mout, mout, mout, a);
+  gemm_tf32x3_kernel<BN, BKB, SPLIT, EPI_ACT><<<grid, kThreads, C::kSmemBytes, stream>>>(mx, mhi, mlo, mout, mout, mout, a);
   return ko::check_launch("ko_linear_f32_packed");
 }
 
@@ -973,7 +956,7 @@ int launch_gemm_ln(const float* x, const float* w_packed, const float* bias, con
   attr[0].val.clusterDim.x = static_cast<unsigned>(cs);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(Roles<EPI_LN, SPLIT>::kThreads);
+  cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
   cfg.attrs = attr;

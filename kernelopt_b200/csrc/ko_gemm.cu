@@ -49,6 +49,7 @@ constexpr int kThreads = 18 * 32;
 constexpr uint32_t kStoreTileBytes = 32 * 32 * 4;                   // one epilogue warp's 32x32 output tile
 constexpr uint32_t kStoreBytes = 8 * kStoreTileBytes;               // 32 KB of staging for the TMA stores
 constexpr size_t kSmemBudget = 224 * 1024 - kStoreBytes;  // stage buffers; staging, barriers, slack on top
+constexpr uint32_t kBarBytes = 512;                        // mbarriers, the TMEM address and the abort flag
 
 // BN: tile width (MMA N). BKB: bytes of K per k-block row (128 -> 128-byte swizzle, 64 -> 64-byte swizzle).
 // SPLIT: accumulate the small hi*lo + lo*hi terms in their own TMEM accumulator and add it to the hi*hi
@@ -92,12 +93,16 @@ struct Cfg {
   static constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
                                         : kTmemNeed <= 256 ? 256 : 512;
   static constexpr uint32_t kTxBytes = kATileBytes + 2 * kBTileBytes;
-  static constexpr size_t kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + kStoreBytes + 256 + kStatBytes;
+  static constexpr size_t kSmemBytes =
+      1024 /*align slack*/ + kStages * kStageBytes + kStoreBytes + kBarBytes + kStatBytes;
+  // Stage st's `full` barrier for k-block it is full[2 st + it % 2] (the split group of it's parity waits on it):
+  // it is used every kFullPeriod k-blocks, so phase = (it / kFullPeriod) & 1.
+  static constexpr uint32_t kFullPeriod = kStages % 2 == 0 ? kStages : 2 * kStages;
   static constexpr uint32_t kSbo = 8 * BKB;                 // bytes between 8-row groups
   static constexpr uint32_t kLayout = BKB == 128 ? 2u : 4u;  // descriptor layout: 128B / 64B swizzle
   static_assert(kStages >= 2, "stage does not fit");
   static_assert(kTmemNeed <= 512, "TMEM overflow");
-  static_assert((3 * kStages + 9) * 8 + 8 <= 256, "barrier area");
+  static_assert((4 * kStages + 10) * 8 <= kBarBytes, "barrier area");
 };
 
 struct GemmArgs {
@@ -230,24 +235,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   // stage st: [x -> hi][lo][W_hi][W_lo]; then 8 epilogue staging tiles; then barriers
   uint8_t* store_smem = smem + S * C::kStageBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(store_smem + kStoreBytes);
-  uint64_t* full = bars;               // TMA landed            (1 arrival + tx bytes)
-  uint64_t* ready = bars + S;          // x split done          (4 arrivals)
-  uint64_t* empty = bars + 2 * S;      // MMAs of stage done    (1 commit)
-  uint64_t* acc_full = bars + 3 * S;   // accumulator complete  (1 commit) x NB
+  // full: TMA landed, one barrier per stage and k-block parity. The two split groups take alternate k-blocks; with
+  // an odd stage count a stage's consecutive uses alternate between the groups, and a group waiting on a shared
+  // barrier for its next use (two phases on) could pass on the other group's phase still pending (a parity wait
+  // cannot tell two phases apart). With one barrier per (stage, parity) each waits only on its own uses, in order.
+  uint64_t* full = bars;               // TMA landed            (1 arrival + tx bytes) x 2S
+  uint64_t* ready = bars + 2 * S;      // x split done          (4 arrivals)
+  uint64_t* empty = bars + 3 * S;      // MMAs of stage done    (1 commit)
+  uint64_t* acc_full = bars + 4 * S;   // accumulator complete  (1 commit) x NB
   uint64_t* acc_empty = acc_full + 2;  // accumulator drained   (4 arrivals) x NB
   uint64_t* mma_done = acc_empty + 2;  // teardown drain        (1 commit)
   uint64_t* a_empty = mma_done + 1;    // TMEM A slot free      (1 commit) x 4
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(a_empty + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // EPI_LN: row statistics (see kLnStatBytes)
-  float2* pair_stats = reinterpret_cast<float2*>(store_smem + kStoreBytes + 256);
+  float2* pair_stats = reinterpret_cast<float2*>(store_smem + kStoreBytes + kBarBytes);
   float2* peer_stats = pair_stats + 2 * 2 * 128;
   uint64_t* peer_bar = reinterpret_cast<uint64_t*>(peer_stats + 2 * 128);
   uint64_t* pair_bar = peer_bar + 2;
   uint64_t* load_bar = pair_bar + 4;
   // EPI_LN: the CTA's BN columns never change (tiles are row blocks), so their bias, scale (1 when absent),
   // gamma and beta are read from global memory once, here, and by the epilogue from shared memory
-  float* ln_par = reinterpret_cast<float*>(store_smem + kStoreBytes + 256 + 6400);  // [4][BN]
+  float* ln_par = reinterpret_cast<float*>(store_smem + kStoreBytes + kBarBytes + 6400);  // [4][BN]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const TileSched<EPI> ts(args, BN);
@@ -256,7 +265,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[2 * s], 1);
+      mbar_init(&full[2 * s + 1], 1);
       mbar_init(&ready[s], 4);
       mbar_init(&empty[s], 1);
     }
@@ -305,11 +315,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      uint32_t issued[S];
+      uint32_t issued[2 * S];
 #pragma unroll
-      for (int s = 0; s < S; ++s) issued[s] = 0;
+      for (int s = 0; s < 2 * S; ++s) issued[s] = 0;
       int st = 0;
       uint32_t phase = 0;
+      uint32_t it = 0;  // running k-block index
       bool ok = true;
       for (int tile = ts.first; tile < num_tiles && ok; tile += ts.step) {
         const int m0 = ts.m0(tile), n0 = ts.n0(tile, BN);
@@ -319,20 +330,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* sbase = smem + st * C::kStageBytes;
-          mbar_arrive_expect_tx(&full[st], C::kTxBytes);
+          const int fb = 2 * st + static_cast<int>(it & 1u);
+          uint64_t* fbar = &full[fb];
+          mbar_arrive_expect_tx(fbar, C::kTxBytes);
           if (args.conv_c > 0) {
             const int cpb = args.conv_c / C::kBK;  // k-blocks per tap
             const int tap = kb / cpb;
-            tma_load_2d(&map_x, &full[st], sbase, (kb - tap * cpb) * C::kBK,
+            tma_load_2d(&map_x, fbar, sbase, (kb - tap * cpb) * C::kBK,
                         m0 + (tap / 3 - 1) * args.conv_w + (tap % 3 - 1));
           } else {
-            tma_load_2d(&map_x, &full[st], sbase, kb * C::kBK, m0);
+            tma_load_2d(&map_x, fbar, sbase, kb * C::kBK, m0);
           }
           constexpr uint32_t kWoff = (C::kTSA ? 1 : 2) * C::kATileBytes;  // W after x (and x_lo, unless TSA)
-          tma_load_2d(&map_whi, &full[st], sbase + kWoff, kb * C::kBK, n0);
-          tma_load_2d(&map_wlo, &full[st], sbase + kWoff + C::kBTileBytes, kb * C::kBK, n0);
+          tma_load_2d(&map_whi, fbar, sbase + kWoff, kb * C::kBK, n0);
+          tma_load_2d(&map_wlo, fbar, sbase + kWoff + C::kBTileBytes, kb * C::kBK, n0);
 #pragma unroll
-          for (int s = 0; s < S; ++s) issued[s] += (s == st);
+          for (int s = 0; s < 2 * S; ++s) issued[s] += (s == fb);
+          ++it;
           if (++st == S) {
             st = 0;
             phase ^= 1u;
@@ -341,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Drain: every load this thread issued must have landed before the CTA may exit.
 #pragma unroll
-      for (int s = 0; s < S; ++s) {
+      for (int s = 0; s < 2 * S; ++s) {
         if (issued[s] == 0) continue;
         volatile int never = 0;
         if (!mbar_wait(&full[s], (issued[s] - 1) & 1u, &never)) *abort_flag = 1;
@@ -424,7 +438,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kRowF4 = BKB / 16;                                    // float4 per tile row
     const bool conv = args.conv_c > 0;
     int st = 0;
-    uint32_t phase = 0;
     uint32_t it = 0;
     bool ok = true;
     for (int tile = ts.first; tile < num_tiles && ok; tile += ts.step) {
@@ -441,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int kb = 0; kb < args.k_blocks; ++kb, ++it) {
         if ((it & 1u) == static_cast<uint32_t>(group)) {
-          if (!mbar_wait(&full[st], phase, abort_flag)) {
+          if (!mbar_wait(&full[2 * st + group], (it / C::kFullPeriod) & 1u, abort_flag)) {
             ok = false;
             break;
           }
@@ -517,10 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(&ready[st]);
           }
         }
-        if (++st == S) {
-          st = 0;
-          phase ^= 1u;
-        }
+        if (++st == S) st = 0;
       }
     }
   } else if constexpr (EPI == EPI_LN) {

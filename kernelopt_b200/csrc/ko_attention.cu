@@ -4,36 +4,45 @@
 //   o[b, i, h, :] = sum_j softmax_j(scale * q[b, i, h, :] . k[b, j, h, :]) v[b, j, h, :]
 //
 // Semantics: the reference's attention calls, mx.fast.scaled_dot_product_attention on head-major q/k/v in the
-// ViT backbone (fast_rfdetr/model.py:107-110 and 119-120, windowed and global layers) and in the decoder's self-attention
-// (self_attn, model.py:232-239, 8 heads of 32), computed in fp32 there. No mask, no dropout.
+// ViT backbone (fast_rfdetr/model.py:107-110 and 119-120, windowed and global layers) and in the decoder's
+// self-attention (self_attn, model.py:232-239, 8 heads of 32), computed in fp32 there. No mask, no dropout.
 //
 // Precision: every operand is split v = hi + lo and the tensor cores accumulate hi*hi + hi*lo + lo*hi in fp32
 // (Ootomo & Yokota's error-compensated 3xTF32). q and k, whose products the exponential amplifies, use
 // hi = tf32_rn(v); p and v use hi = v itself, which the tensor core reads truncated to tf32, and lo = the exact
-// remainder below that truncation (two operations per element instead of three; error below 2^-20 per term). The softmax runs in
-// fp32 registers with the running maximum / running sum of the online (flash) formulation; each key block's
-// P.V product lands in a fresh tensor-memory accumulator and is added into the fp32 output row in registers,
-// so the long sum over keys is a plain fp32 register sum, not a tensor-core accumulation.
+// remainder below that truncation (two operations per element instead of three; error below 2^-20 per term). The
+// softmax runs in fp32 registers with the running maximum / running sum of the online (flash) formulation; each
+// key block's P.V product lands in a fresh tensor-memory accumulator and is added into the fp32 output row in
+// registers, so the long sum over keys is a plain fp32 register sum, not a tensor-core accumulation.
 //
-// Kernel structure: one CTA per (128-query tile, head, batch item); 13 warps.
-//   warp 0      allocates tensor memory; one lane issues the MMAs:
-//                 S  = Q K_j^T      (M 128, N 128 keys, K = head dim;  A, B in shared memory)
-//                 O_j = P_j V_j     (M 128, N = head dim, K = 128 keys; A = P in tensor memory, B in shared)
+// Kernel structure: a pair of CTAs (a cluster of two on one GPU) per (two 128-query tiles, head, batch item); 13
+// warps each. The pair runs the 5th-generation tensor cores of two SMs as one (tcgen05 cta_group::2): every MMA
+// has M = 256, rows 0-127 being the leader's (rank 0) query tile and 128-255 the peer's, each CTA holding its own
+// A rows and HALF of B at the same shared-memory offset and receiving its 128 rows of the product in its own tensor
+// memory. So each SM loads, splits and stores only half of each k / v tile, and its tensor core reads only half of
+// each B operand; and the halves fit twice in shared memory, so the loaders write block j + 1 while block j's
+// MMAs read block j (with one buffer, each block's k and v writes waited for the previous block's MMAs).
+//   warp 0      allocates the pair's tensor memory; in the leader, one lane issues the MMAs of both CTAs:
+//                 S  = Q K_j^T      (M 256, N = 128 keys, K = head dim;  A, B in shared memory)
+//                 O_j = P_j V_j     (M 256, N = head dim, K = 128 keys; A = P in tensor memory, B in shared)
 //   warps 1-4   softmax + output: one thread per query row. Reads S from tensor memory, updates the row's running
 //               max / sum, writes P (hi and lo) back into tensor memory for the P.V MMA, then adds O_j into the
 //               output row it keeps in registers. At the end divides by the sum and stores the row.
-//   warps 5-12  loaders: the q tile and the first k tile arrive by TMA and are split in place, q by warps 9-12 and
-//               k by warps 5-8 at the same time; the other key blocks stream from global memory (128-bit loads;
-//               warps 5-8 stream k, 9-12 stream v, each holding the next key block in registers while the current
-//               one is in use), split into hi / lo and written into shared memory in the MMA's 128-byte-swizzled
-//               K-major layout. v is
-//               written transposed (head dim x keys), the K-major form of the P.V product's B operand.
-// Tensor memory (512 columns): two S / P_hi buffers [0,256), P_lo [256,384), two O_j buffers of HD columns from
-// 384. With two S buffers the tensor cores compute S_{j+1} while the softmax warps work on block j, and P_j.V_j
-// issues its P_lo products first and then frees the one P_lo buffer, so the softmax warps write P_{j+1} while
-// the P_hi products of block j run (the softmax of one block overlaps the tensor-core work of the previous).
-// Every wait on an mbarrier is bounded (2 s); on timeout the CTA stops, drains its MMAs, frees tensor memory and
-// reports KO_ERR_DEVICE_TIMEOUT through dev_status.
+//   warps 5-12  loaders: the q tile and this CTA's half of the first k tile arrive by TMA and are split in place,
+//               q by warps 9-12 and k by warps 5-8 at the same time; later key blocks stream from global memory
+//               (128-bit loads; warps 5-8 stream this CTA's k rows, 9-12 its v columns, each holding the next
+//               half tile in registers), split into hi / lo and written into one of two shared-memory buffers in
+//               the MMA's 128-byte-swizzled K-major layout. v is written transposed (head dim x keys), the K-major
+//               form of the P.V product's B operand.
+// A query tile count that is odd gets one more tile of padding rows (zero queries, never stored).
+// Tensor memory (512 columns per CTA): two S / P_hi buffers [0,256), P_lo [256,384), two O_j buffers of HD columns
+// from 384. With two S buffers the tensor cores compute S_{j+1} while the softmax warps work on block j, and
+// P_j.V_j issues its P_lo products first and then frees the one P_lo buffer, so the softmax warps write P_{j+1}
+// while the P_hi products of block j run (the softmax of one block overlaps the tensor-core work of the previous).
+// Barriers that the leader's MMA lane waits on count arrivals from both CTAs (the peer arrives through the
+// cluster-mapped address of the leader's barrier, after the same proxy / tensor-memory fences as a local arrival);
+// each MMA completion is committed to the same barrier in both CTAs. Every wait on an mbarrier is bounded (2 s); on
+// timeout the CTA stops, drains its MMAs, frees tensor memory and reports KO_ERR_DEVICE_TIMEOUT through dev_status.
 #include <algorithm>
 #include <climits>
 #include <string>
@@ -44,8 +53,9 @@ namespace {
 
 using namespace kodev;
 
-constexpr int BQ = 128;    // query rows per CTA (MMA M)
-constexpr int BKEY = 128;  // keys per block (MMA N of S, K of P.V)
+constexpr int BQ = 128;            // query rows per CTA (half of the pair's MMA M)
+constexpr int BKEY = 128;          // keys per block (MMA N of S, K of P.V)
+constexpr int KHALF = BKEY / 2;    // k rows of a block held by one CTA of the pair (at most)
 constexpr int kLoadWarp0 = 5;
 constexpr int kLoadThreads = 256;
 constexpr int kThreads = 13 * 32;
@@ -70,14 +80,14 @@ template <int HD>
 struct AttnCfg {
   static constexpr int kKB = HD / 32;                          // 128-byte k-blocks of a q / k row
   static constexpr uint32_t kQBytes = BQ * HD * 4;             // one of Q_hi / Q_lo
-  static constexpr uint32_t kKBytes = BKEY * HD * 4;           // one of K_hi / K_lo
-  static constexpr uint32_t kVBytes = HD * BKEY * 4;           // one of Vt_hi / Vt_lo
+  static constexpr uint32_t kKBytes = KHALF * HD * 4;          // one of K_hi / K_lo of this CTA's k rows
+  static constexpr uint32_t kVBytes = (HD / 2) * BKEY * 4;     // one of Vt_hi / Vt_lo of this CTA's v columns
+  static constexpr uint32_t kKBufBytes = 2 * kKBytes;          // a k buffer: [K_hi][K_lo]
+  static constexpr uint32_t kVBufBytes = 2 * kVBytes;          // a v buffer: [Vt_hi][Vt_lo]
   static constexpr uint32_t kOffQlo = kQBytes;
-  static constexpr uint32_t kOffKhi = 2 * kQBytes;
-  static constexpr uint32_t kOffKlo = kOffKhi + kKBytes;
-  static constexpr uint32_t kOffVhi = kOffKlo + kKBytes;
-  static constexpr uint32_t kOffVlo = kOffVhi + kVBytes;
-  static constexpr uint32_t kOffBars = kOffVlo + kVBytes;
+  static constexpr uint32_t kOffK = 2 * kQBytes;               // two k buffers (block j in buffer j & 1)
+  static constexpr uint32_t kOffV = kOffK + 2 * kKBufBytes;    // two v buffers
+  static constexpr uint32_t kOffBars = kOffV + 2 * kVBufBytes;
   // At least 120 KB even where the tiles need less (head dim 32), so that one CTA per SM holds all 512 tensor-
   // memory columns and no second CTA waits in tcgen05.alloc.
   static constexpr size_t kSmemNeed = 1024 + kOffBars + 256;
@@ -133,6 +143,46 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok);
 }
 
+// tcgen05 of a CTA pair (cta_group::2): every tcgen05 operation of the kernel names the pair. The allocation is made
+// by warp 0 of both CTAs with the same destination slot.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D (+)= A B over the pair, A and B from shared memory (elected lane of the calling warp).
+__device__ __forceinline__ void mma_pair_tf32_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// The same with A in tensor memory (each CTA's 128 lanes).
+__device__ __forceinline__ void mma_pair_tf32_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                   uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on `bar` in both CTAs of the pair when every MMA issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit_pair_w(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b16 mask;\n\tmov.b16 mask, 3;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], mask;\n\t}"
+      ::"r"(smem_addr(bar))
+      : "memory");
+}
+
 // The part of v below its tf32 truncation: v - (v with the low 13 mantissa bits cleared), exact in fp32. P is kept
 // as v in the P_hi slot (the tensor core reads a tf32 operand from the top 19 bits of the word, i.e. truncates)
 // and this tail in P_lo, so P = P_hi + P_lo exactly before the MMA truncates P_lo (an error below 2^-20 P).
@@ -160,155 +210,175 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
-  uint64_t* q_ready = bars + 0;   // q tile split            (4 v-loader warps)
-  uint64_t* k_full = bars + 1;    // k tile written          (4 k-loader warps)
-  uint64_t* v_full = bars + 3;    // v tile written          (4 v-loader warps)
-  uint64_t* s_full = bars + 5;    // S_j complete, x2        (1 commit)
-  uint64_t* p_full = bars + 7;    // P_j written             (4 softmax warps)
-  uint64_t* o_full = bars + 8;    // O_j complete, x2        (1 commit)
-  uint64_t* o_empty = bars + 10;  // O_j consumed, x2        (4 softmax warps)
-  uint64_t* mma_done = bars + 12;
-  uint64_t* plo_free = bars + 13;  // P_j.V_j's P_lo products done (1 commit)
+  // Barriers the leader's MMA warp waits on collect arrivals from both CTAs of the pair; the MMA commits arrive on
+  // the same barrier in both CTAs (multicast).
+  uint64_t* q_ready = bars + 0;   // q tile split            (4 v-loader warps x 2 CTAs, leader)
+  uint64_t* k_full = bars + 1;    // k half tile written, x2 (4 k-loader warps x 2 CTAs, leader)
+  uint64_t* v_full = bars + 3;    // v half tile written, x2 (4 v-loader warps x 2 CTAs, leader)
+  uint64_t* s_full = bars + 5;    // S_j complete, x2        (1 commit, both CTAs)
+  uint64_t* p_full = bars + 7;    // P_j written             (4 softmax warps x 2 CTAs, leader)
+  uint64_t* o_full = bars + 8;    // O_j complete, x2        (1 commit, both CTAs)
+  uint64_t* mma_done = bars + 12;  // every MMA complete      (1 commit, both CTAs)
+  uint64_t* plo_free = bars + 13;  // P_j.V_j's P_lo products done (1 commit, both CTAs)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
-  uint64_t* q_tma = bars + 15;     // q tile landed (fp32) (1 arrival + tx bytes)
-  uint64_t* k0_tma = bars + 16;    // first k tile landed   (1 arrival + tx bytes)
+  uint64_t* q_tma = bars + 15;     // q tile landed (fp32)     (1 arrival + tx bytes)
+  uint64_t* k0_tma = bars + 16;    // first k half tile landed (1 arrival + tx bytes)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * BQ;
+  const uint32_t rank = cluster_ctarank();  // 0: the leader, which issues the pair's MMAs
   const int nkb = a.n_kblocks;
+  // keys of block j, the S MMA's N (keys rounded up to 16) and this CTA's share of the block's k rows (N / 2,
+  // starting at rank * N / 2)
+  auto keys_of = [&](int j) { return min(BKEY, a.L - j * BKEY); };
+  auto n_of = [&](int j) { return (keys_of(j) + 15) & ~15; };
+  // Arrive on the leader's copy of a barrier (this CTA's own when it is the leader): the leader's barrier area is
+  // mapped once, the barrier's offset within it is a constant. The arrival has the default (CTA-scope release)
+  // semantics; a cluster-scope release costs a cluster-wide memory barrier per arrival, which stalled the
+  // softmax and loader warps (10 % of the kernel's time).
+  const uint32_t leader_bars = cluster_map(smem_addr(bars), 0);
+  auto arrive_leader = [&](uint64_t* bar) {
+    const uint32_t addr = leader_bars + static_cast<uint32_t>(reinterpret_cast<uint8_t*>(bar) -
+                                                               reinterpret_cast<uint8_t*>(bars));
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_ready, 4);
-    mbar_init(k_full, 4);
-    mbar_init(v_full, 4);
-    mbar_init(p_full, 4);
+    mbar_init(q_ready, 8);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 8);
+      mbar_init(&v_full[i], 8);
       mbar_init(&s_full[i], 1);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 4);
     }
+    mbar_init(p_full, 8);
     mbar_init(mma_done, 1);
     mbar_init(plo_free, 1);
     mbar_init(q_tma, 1);
     mbar_init(k0_tma, 1);
     *abort_flag = 0;
     fence_barrier_init();
-    // The q tile and the first k tile come in by TMA at once (fp32, in the 128-byte-swizzled K-major layout the
-    // MMAs read, one 32-column box per 128-byte k-block); the loaders split them in place.
+    // The q tile and this CTA's half of the first k tile come in by TMA at once (fp32, in the 128-byte-swizzled
+    // K-major layout the MMAs read, one 32-column box per 128-byte k-block); the loaders split them in place.
     const int bq = a.q_bstride ? b : 0, bk = a.k_bstride ? b : 0;
     mbar_arrive_expect_tx(q_tma, C::kQBytes);
     mbar_arrive_expect_tx(k0_tma, C::kKBytes);
+    const int k0_row = static_cast<int>(rank) * (n_of(0) / 2);
 #pragma unroll
     for (int kb = 0; kb < C::kKB; ++kb) {
       tma_load_3d(&map_q, q_tma, smem + kb * (BQ * 128), h * HD + kb * 32, q0, bq);
-      tma_load_3d(&map_k, k0_tma, smem + C::kOffKhi + kb * (BKEY * 128), h * HD + kb * 32, 0, bk);
+      tma_load_3d(&map_k, k0_tma, smem + C::kOffK + kb * (KHALF * 128), h * HD + kb * 32, k0_row, bk);
     }
   }
   if (warp == 0) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // both CTAs' barriers are initialised before any arrival from the peer
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- MMA issuer ----------------
-    // Order on the tensor pipe: S_0, then per block j: S_{j+1} (into the other S buffer, overlapping softmax_j),
-    // P_j.V_j. S_{j+1} reuses the buffer of P_{j-1}, so it waits for P_{j-1}.V_{j-1} to complete.
-    // The whole warp runs this loop with the same values in every lane; one elected lane issues each MMA.
-    {
-      // Descriptors are built once; an MMA's operand is its tile's descriptor plus the byte offset / 16 (the
-      // start-address field; shared addresses stay below 2^18 bytes, so the field cannot overflow).
+    if (rank == 0) {
+      // ---------------- MMA issuer (leader) ----------------
+      // Order on the tensor pipes of the pair: S_0, then per block j: S_{j+1} (into the other S buffer,
+      // overlapping softmax_j), P_j.V_j. S_{j+1} reuses the buffer of P_{j-1}, so it waits for P_{j-1}.V_{j-1}.
+      // Each MMA has M = 256: rows 0-127 are the leader's query tile, 128-255 the peer's, each CTA holding its A
+      // rows (q, or P in its tensor memory) and half of B (k rows, or v columns) at the same shared-memory offset,
+      // and receiving its 128 rows of the product in its own tensor memory.
+      // The whole warp runs this loop with the same values in every lane; one elected lane issues each MMA.
       const uint32_t sb = smem_addr(smem);
-      constexpr uint32_t idesc_o = idesc_tf32(BQ, HD);
+      constexpr uint32_t idesc_o = idesc_tf32(2 * BQ, HD);
       const uint64_t dq_hi = smem_desc_k_sw128(sb), dq_lo = smem_desc_k_sw128(sb + C::kOffQlo);
-      const uint64_t dk_hi = smem_desc_k_sw128(sb + C::kOffKhi), dk_lo = smem_desc_k_sw128(sb + C::kOffKlo);
-      const uint64_t dv_hi = smem_desc_k_sw128(sb + C::kOffVhi), dv_lo = smem_desc_k_sw128(sb + C::kOffVlo);
-      // A short last key block (e.g. 17 of the 401 keys of a window) gets MMAs only as wide / deep as its keys:
-      // N = keys rounded up to 16 for S, K = keys rounded up to 8 for P.V.
-      auto keys_of = [&](int j) { return min(BKEY, a.L - j * BKEY); };
       auto issue_s = [&](int j) {  // S_j = Q K_j^T into S buffer j & 1
         const uint32_t d = tmem + kColS + static_cast<uint32_t>(j & 1) * BKEY;
-        const uint32_t idesc_s = idesc_tf32(BQ, (keys_of(j) + 15) & ~15);
+        const uint32_t idesc_s = idesc_tf32(2 * BQ, n_of(j));
+        const uint32_t kb0 = sb + C::kOffK + static_cast<uint32_t>(j & 1) * C::kKBufBytes;
+        const uint64_t dk_hi = smem_desc_k_sw128(kb0), dk_lo = smem_desc_k_sw128(kb0 + C::kKBytes);
 #pragma unroll
         for (int s = 0; s < C::kKB * 4; ++s) {  // 8-wide k-steps over the head dimension
-          const uint64_t off = static_cast<uint64_t>(((s >> 2) * (BQ * 128) + (s & 3) * 32) >> 4);
-          mma_tf32_w(d, dq_lo + off, dk_hi + off, idesc_s, s == 0 ? 0u : 1u);
-          mma_tf32_w(d, dq_hi + off, dk_lo + off, idesc_s, 1u);
-          mma_tf32_w(d, dq_hi + off, dk_hi + off, idesc_s, 1u);
+          const uint64_t qoff = static_cast<uint64_t>(((s >> 2) * (BQ * 128) + (s & 3) * 32) >> 4);
+          const uint64_t koff = static_cast<uint64_t>(((s >> 2) * (KHALF * 128) + (s & 3) * 32) >> 4);
+          mma_pair_tf32_w(d, dq_lo + qoff, dk_hi + koff, idesc_s, s == 0 ? 0u : 1u);
+          mma_pair_tf32_w(d, dq_hi + qoff, dk_lo + koff, idesc_s, 1u);
+          mma_pair_tf32_w(d, dq_hi + qoff, dk_hi + koff, idesc_s, 1u);
         }
-        mma_commit_w(&s_full[j & 1]);  // the k loaders wait on it too (S_j done = k tile j free)
+        mma_commit_pair_w(&s_full[j & 1]);  // the k loaders wait on it too (S_j done = k buffer j & 1 free)
       };
-      bool ok = warp_wait(q_ready, 0, abort_flag) && warp_wait(k_full, 0, abort_flag);
+      bool ok = warp_wait(q_ready, 0, abort_flag) && warp_wait(&k_full[0], 0, abort_flag);
       if (ok) {
         tc_fence_after();
         issue_s(0);
       }
       for (int j = 0; j < nkb && ok; ++j) {
         if (j + 1 < nkb) {
-          if (!warp_wait(k_full, static_cast<uint32_t>(j + 1) & 1u, abort_flag)) break;
-          if (j >= 1 && !warp_wait(&o_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag)) break;
+          const uint32_t kpar = static_cast<uint32_t>((j + 1) >> 1) & 1u;
+          const uint32_t opar = static_cast<uint32_t>((j - 1) >> 1) & 1u;
+          if (!warp_wait(&k_full[(j + 1) & 1], kpar, abort_flag)) break;
+          if (j >= 1 && !warp_wait(&o_full[(j - 1) & 1], opar, abort_flag)) break;
           tc_fence_after();
           issue_s(j + 1);
         }
-        // O_j = P_j V_j into O buffer j & 1, once P_j is written, V_j landed and the buffer was consumed
+        // O_j = P_j V_j into O buffer j & 1, once P_j is written and V_j landed. The buffer held O_{j-2}, which
+        // every softmax warp read (add_block(j - 2)) before it wrote P_j: p_full covers it.
         if (!warp_wait(p_full, static_cast<uint32_t>(j) & 1u, abort_flag) ||
-            !warp_wait(v_full, static_cast<uint32_t>(j) & 1u, abort_flag) ||
-            !warp_wait(&o_empty[j & 1], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, abort_flag))
+            !warp_wait(&v_full[j & 1], static_cast<uint32_t>(j >> 1) & 1u, abort_flag))
           break;
         tc_fence_after();
         const uint32_t d = tmem + kColO + static_cast<uint32_t>(j & 1) * HD;
         const uint32_t p_hi = tmem + kColS + static_cast<uint32_t>(j & 1) * BKEY;
+        const uint32_t vb0 = sb + C::kOffV + static_cast<uint32_t>(j & 1) * C::kVBufBytes;
+        const uint64_t dv_hi = smem_desc_k_sw128(vb0), dv_lo = smem_desc_k_sw128(vb0 + C::kVBytes);
         const int ksteps = (keys_of(j) + 7) >> 3;
         // The P_lo products first, then a commit that hands the P_lo columns back to the softmax warps: they
         // write P_{j+1} while the P_hi products of this block (two thirds of its MMAs) still run. A full block's
-        // MMAs are issued from fully unrolled code: a 128 x HD x 8 product takes the tensor pipe only 32 cycles
-        // (HD 64), and a rolled loop's per-MMA address arithmetic would make the issue, not the pipe, the limit.
+        // MMAs are issued from fully unrolled code (a rolled loop's address arithmetic would make the issue, not
+        // the pipe, the limit).
         if (ksteps == BKEY / 8) {
 #pragma unroll
           for (int kk = 0; kk < BKEY / 8; ++kk) {  // 8 keys per k-step
-            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
-            mma_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
+            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD / 2 * 128) + (kk & 3) * 32) >> 4);
+            mma_pair_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
           }
-          mma_commit_w(plo_free);
+          mma_commit_pair_w(plo_free);
 #pragma unroll
           for (int kk = 0; kk < BKEY / 8; ++kk) {
-            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
-            mma_tf32_ts_w(d, p_hi + 8 * kk, dv_lo + off, idesc_o, 1u);
-            mma_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + off, idesc_o, 1u);
+            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD / 2 * 128) + (kk & 3) * 32) >> 4);
+            mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_lo + off, idesc_o, 1u);
+            mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + off, idesc_o, 1u);
           }
         } else {  // a short last block
 #pragma unroll 1
           for (int kk = 0; kk < ksteps; ++kk) {
-            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
-            mma_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
+            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD / 2 * 128) + (kk & 3) * 32) >> 4);
+            mma_pair_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
           }
-          mma_commit_w(plo_free);
+          mma_commit_pair_w(plo_free);
 #pragma unroll 1
           for (int kk = 0; kk < ksteps; ++kk) {
-            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD * 128) + (kk & 3) * 32) >> 4);
-            mma_tf32_ts_w(d, p_hi + 8 * kk, dv_lo + off, idesc_o, 1u);
-            mma_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + off, idesc_o, 1u);
+            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD / 2 * 128) + (kk & 3) * 32) >> 4);
+            mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_lo + off, idesc_o, 1u);
+            mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + off, idesc_o, 1u);
           }
         }
-        // One commit per event: the v loaders wait on o_full as well (P_j.V_j done = v tile j free).
-        mma_commit_w(&o_full[j & 1]);
+        // One commit per event: the v loaders wait on o_full as well (P_j.V_j done = v buffer j & 1 free).
+        mma_commit_pair_w(&o_full[j & 1]);
       }
-      // Drain: every MMA this warp issued completes before tensor memory is released.
-      mma_commit_w(mma_done);
-      volatile int never = 0;
-      if (!warp_wait(mma_done, 0, &never)) *abort_flag = 1;
+      // Drain: every MMA this warp issued completes before either CTA releases its tensor memory.
+      mma_commit_pair_w(mma_done);
     }
+    volatile int never = 0;
+    if (!warp_wait(mma_done, 0, &never)) *abort_flag = 1;
   } else if (warp < kLoadWarp0) {
     // ---------------- softmax + output, one thread per query row ----------------
-    // Block j, two passes over S_j in tensor memory (a 16-column load costs about 9 cycles): the first finds the
-    // row maximum, which sets the block's offset m = max(m, block maximum) (online softmax, P <= 1); once
-    // P_{j-1}.V_{j-1}'s P_lo products are done (the P_lo columns are free) the second turns each 16-key chunk
-    // into P = exp2(S * c - m), written as P itself and its tf32 tail. The max pass overlaps that wait. Then, once
-    // all of P_{j-1}.V_{j-1} is complete, o = o * alpha + that block's product.
+    // Block j, two passes over S_j in tensor memory: the first finds the row maximum, which sets the block's
+    // offset m = max(m, block maximum) (online softmax, P <= 1); once P_{j-1}.V_{j-1}'s P_lo products are done
+    // (the P_lo columns are free) the second turns each 16-key chunk into P = exp2(S * c - m), written as P
+    // itself and its tf32 tail. The max pass overlaps that wait. Then, once all of P_{j-1}.V_{j-1} is complete,
+    // o = o * alpha + that block's product.
     const int quad = warp & 3;  // tensor-memory lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
@@ -329,9 +399,6 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
 #pragma unroll
         for (int e = 0; e < 16; ++e) o[16 * c + e] = fmaf(o[16 * c + e], alpha, __uint_as_float(r[e]));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[jb & 1]);
       return true;
     };
     for (int j = 0; j < nkb; ++j) {
@@ -342,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
       tc_fence_after();
       const uint32_t srow = trow + kColS + static_cast<uint32_t>(j & 1) * BKEY;
       const uint32_t plrow = trow + kColPlo;
-      const int valid = min(BKEY, a.L - j * BKEY);
+      const int valid = keys_of(j);
       const int chunks = (valid + 15) >> 4;  // 16-column chunks that hold keys of this block
       // pass 1: the block's row maximum
       float mx = -INFINITY;
@@ -394,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
       m = mb;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) arrive_leader(p_full);
       if (j >= 1 && !add_block(j - 1, alpha_prev)) {
         ok = false;
         break;
@@ -413,12 +480,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
     }
   } else {
     // ---------------- loaders ----------------
-    // The q tile and the first k tile come by TMA; the v group (warps 9-12) splits q in place while the k group
-    // (warps 5-8) splits the first k tile, so S_0 waits for one split, not two in a row. Then warps 5-8 stream the
-    // k tiles and warps 9-12 the v tiles, each group holding its next tile in registers while the current one is
-    // in use.
+    // The q tile and this CTA's half of the first k tile come by TMA; the v group (warps 9-12) splits q in place
+    // while the k group (warps 5-8) splits the k half, so S_0 waits for one split, not two in a row. Then warps
+    // 5-8 stream this CTA's k halves (its N / 2 keys of each block) and warps 9-12 its v halves (all keys of a
+    // block, head-dim columns [rank * HD / 2, (rank + 1) * HD / 2)), into alternating buffers, each group holding
+    // its next half tile in registers while the current one is written.
     const int t = threadIdx.x - kLoadWarp0 * 32;  // 0..255
-    constexpr int Q4 = HD / 4;                   // float4 per row
+    constexpr int Q4 = HD / 4;                   // float4 per q / k row
     // hi in place, lo at the same offset in the lo buffer (the split is elementwise: any cover of the tile works)
     auto split_in_place = [&](uint32_t off_hi, uint32_t off_lo, int n4, int tid, int nthreads) {
       for (int i = tid; i < n4; i += nthreads) {
@@ -435,98 +503,106 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
       fence_proxy_async_smem();
       __syncwarp();
     };
-    constexpr int kGroup = kLoadThreads / 2;       // 128 threads per group
-    constexpr int kTileChunks = BKEY * HD / 4 / kGroup;
+    constexpr int kGroup = kLoadThreads / 2;  // 128 threads per group
+    constexpr int kTileChunks = KHALF * HD / 4 / kGroup;  // float4 per thread of a half tile (k or v)
     const int g = t & (kGroup - 1);
-    auto write_q = [&]() -> bool {
-      if (!mbar_wait(q_tma, 0, abort_flag)) return false;
-      split_in_place(0, C::kOffQlo, static_cast<int>(C::kQBytes / 16), g, kGroup);
-      if (lane == 0) mbar_arrive(q_ready);
-      return true;
-    };
     float4 reg[kTileChunks];
     if (t < kGroup) {
-      // k tiles: row-major chunks (a warp reads whole rows), stored K-major with the 128-byte swizzle
+      // k halves: row-major chunks (a warp reads whole rows), stored K-major with the 128-byte swizzle
       const float* kbp = a.k + static_cast<int64_t>(b) * a.k_bstride + h * HD;
       auto load = [&](int j) {
+        const int half = n_of(j) / 2, r0 = j * BKEY + static_cast<int>(rank) * half;
 #pragma unroll
         for (int i = 0; i < kTileChunks; ++i) {
-          const int idx = i * kGroup + g, kr = j * BKEY + idx / Q4, kc = idx % Q4;
-          reg[i] = kr < a.L ? __ldg(reinterpret_cast<const float4*>(kbp + static_cast<int64_t>(kr) * a.k_row) + kc)
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+          const int idx = i * kGroup + g, r = idx / Q4, kr = r0 + r, kc = idx % Q4;
+          reg[i] = r < half && kr < a.L
+                       ? __ldg(reinterpret_cast<const float4*>(kbp + static_cast<int64_t>(kr) * a.k_row) + kc)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       };
-      // The first k tile is split as soon as it lands (the v group splits q meanwhile); the prefetch of the
-      // next tile into registers follows, so that its loads do not compete with the split.
+      // The first k half is split as soon as it lands (the v group splits q meanwhile); the prefetch of the
+      // next one into registers follows, so that its loads do not compete with the split.
       bool kok = mbar_wait(k0_tma, 0, abort_flag);
       if (kok) {
-        split_in_place(C::kOffKhi, C::kOffKlo, static_cast<int>(C::kKBytes / 16), g, kGroup);
-        if (lane == 0) mbar_arrive(k_full);
+        split_in_place(C::kOffK, C::kOffK + C::kKBytes, static_cast<int>(C::kKBytes / 16), g, kGroup);
+        if (lane == 0) arrive_leader(&k_full[0]);
       }
       if (nkb > 1) load(1);
       for (int j = 1; j < nkb && kok; ++j) {
-        // k tile j overwrites tile j-1: S_{j-1} must be complete
-        if (!mbar_wait(&s_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag)) break;
+        // k buffer j & 1 held tile j - 2: S_{j-2} must be complete
+        if (j >= 2 && !mbar_wait(&s_full[j & 1], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag)) break;
+        const uint32_t kbuf = C::kOffK + static_cast<uint32_t>(j & 1) * C::kKBufBytes;
 #pragma unroll
         for (int i = 0; i < kTileChunks; ++i) {
           const int idx = i * kGroup + g, r = idx / Q4, c = idx % Q4;
-          const uint32_t off = (c >> 3) * (BKEY * 128) + sw128(r, c & 7);
+          const uint32_t off = (c >> 3) * (KHALF * 128) + sw128(r, c & 7);
           float4 hi, lo;
           split_tf32(reg[i].x, hi.x, lo.x);
           split_tf32(reg[i].y, hi.y, lo.y);
           split_tf32(reg[i].z, hi.z, lo.z);
           split_tf32(reg[i].w, hi.w, lo.w);
-          *reinterpret_cast<float4*>(smem + C::kOffKhi + off) = hi;
-          *reinterpret_cast<float4*>(smem + C::kOffKlo + off) = lo;
+          *reinterpret_cast<float4*>(smem + kbuf + off) = hi;
+          *reinterpret_cast<float4*>(smem + kbuf + C::kKBytes + off) = lo;
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(k_full);
+        if (lane == 0) arrive_leader(&k_full[j & 1]);
         if (j + 1 < nkb) load(j + 1);
       }
     } else {
-      // v tiles: a warp reads 32 consecutive keys of one 4-wide column group and writes them transposed
-      // (head dim x keys, K-major, 128-byte swizzle): every scalar store of the warp fills one 128-byte row.
-      const float* vbp = a.v + static_cast<int64_t>(b) * a.v_bstride + h * HD;
+      // v halves: a thread reads one key's HD / 2 columns of this CTA's half (8 or 4 float4) and writes them
+      // transposed (head dim x keys, K-major, 128-byte swizzle): every scalar store of a warp fills one 128-byte
+      // row (32 consecutive keys of one head-dim column).
+      const float* vbp = a.v + static_cast<int64_t>(b) * a.v_bstride + h * HD + static_cast<int>(rank) * (HD / 2);
       auto load = [&](int j) {
+        const int vr = j * BKEY + g;
 #pragma unroll
-        for (int i = 0; i < kTileChunks; ++i) {
-          const int idx = i * kGroup + g, vr = j * BKEY + (idx & (BKEY - 1)), vc = idx / BKEY;
-          reg[i] = vr < a.L ? __ldg(reinterpret_cast<const float4*>(vbp + static_cast<int64_t>(vr) * a.v_row) + vc)
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+        for (int i = 0; i < kTileChunks; ++i)
+          reg[i] = vr < a.L ? __ldg(reinterpret_cast<const float4*>(vbp + static_cast<int64_t>(vr) * a.v_row) + i)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);  // keys past the end: P is 0 there, v must be finite
       };
-      const bool vok = write_q();
+      // q: split in place as soon as it lands
+      bool vok = mbar_wait(q_tma, 0, abort_flag);
+      if (vok) {
+        split_in_place(0, C::kOffQlo, static_cast<int>(C::kQBytes / 16), g, kGroup);
+        if (lane == 0) arrive_leader(q_ready);
+      }
       load(0);
       for (int j = 0; j < nkb && vok; ++j) {
-        // v tile j overwrites tile j-1: P_{j-1}.V_{j-1} must be complete
-        if (j >= 1 && !mbar_wait(&o_full[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag)) break;
+        // v buffer j & 1 held tile j - 2: P_{j-2}.V_{j-2} must be complete
+        if (j >= 2 && !mbar_wait(&o_full[j & 1], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag)) break;
+        const uint32_t vbuf = C::kOffV + static_cast<uint32_t>(j & 1) * C::kVBufBytes;
+        const int key = g;
+        const uint32_t base = (key >> 5) * (HD / 2 * 128) + ((key & 3) << 2);
 #pragma unroll
         for (int i = 0; i < kTileChunks; ++i) {
-          const int idx = i * kGroup + g, key = idx & (BKEY - 1), dq = idx / BKEY;
-          const uint32_t base = (key >> 5) * (HD * 128) + ((key & 3) << 2);
           const float* src = reinterpret_cast<const float*>(&reg[i]);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int d = 4 * dq + e;
+            const int d = 4 * i + e;  // head-dim column within this CTA's half
             const uint32_t off = base + sw128(d, (key & 31) >> 2);
             const float hi = src[e], lo = tf32_tail(src[e]);  // v itself as hi: P.V errors are not amplified
-            *reinterpret_cast<float*>(smem + C::kOffVhi + off) = hi;
-            *reinterpret_cast<float*>(smem + C::kOffVlo + off) = lo;
+            *reinterpret_cast<float*>(smem + vbuf + off) = hi;
+            *reinterpret_cast<float*>(smem + vbuf + C::kVBytes + off) = lo;
           }
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(v_full);
+        if (lane == 0) arrive_leader(&v_full[j & 1]);
         if (j + 1 < nkb) load(j + 1);
       }
     }
   }
 
+  // Neither CTA leaves while the other may still arrive on its barriers or (the leader's MMAs) read its shared and
+  // tensor memory: every MMA is complete (mma_done, waited by warp 0 of each CTA above) and every thread of the
+  // pair is past its last arrival.
+  tc_fence_before();
   __syncthreads();
+  cluster_sync();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc_pair(tmem, kTmemCols);
   }
   if (threadIdx.x == 0 && *abort_flag && a.dev_status) atomicExch(a.dev_status, KO_ERR_DEVICE_TIMEOUT);
 }
@@ -574,7 +650,7 @@ extern "C" int ko_attention_f32(const float* q, const float* k, const float* v, 
   a.dev_status = dev_status;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // q and k tiles by TMA: [batch][L][heads * head_dim] with the caller's strides, boxes of 32 columns x 128 rows
-  // (a stride of 0 between batch items maps every item to plane 0)
+  // (q) and x 64 rows (a CTA's half of a k tile); a stride of 0 between batch items maps every item to plane 0
   CUtensorMap mq, mk;
   const uint64_t width = static_cast<uint64_t>(heads * head_dim);
   int rc = ko::make_tmap_3d_f32(&mq, q, q_bstride ? batch : 1, L, width, q_row,
@@ -582,27 +658,45 @@ extern "C" int ko_attention_f32(const float* q, const float* k, const float* v, 
                                 "ko_attention_f32 q");
   if (rc) return rc;
   rc = ko::make_tmap_3d_f32(&mk, k, k_bstride ? batch : 1, L, width, k_row, k_bstride ? k_bstride : k_row * L + 4,
-                            BKEY, 32, CU_TENSOR_MAP_SWIZZLE_128B, "ko_attention_f32 k");
+                            KHALF, 32, CU_TENSOR_MAP_SWIZZLE_128B, "ko_attention_f32 k");
   if (rc) return rc;
-  dim3 grid(static_cast<unsigned>((L + BQ - 1) / BQ), static_cast<unsigned>(heads), static_cast<unsigned>(batch));
+  // query tiles in pairs (clusters of two along x); an odd count gets one tile of padding rows
+  const int64_t qtiles = (L + BQ - 1) / BQ;
+  dim3 grid(static_cast<unsigned>((qtiles + 1) & ~int64_t(1)), static_cast<unsigned>(heads),
+            static_cast<unsigned>(batch));
   const ko::DeviceInfo* dinfo = nullptr;
   rc = ko::device_or_fail(&dinfo, who);
   if (rc) return rc;
   const ko::DeviceInfo& info = *dinfo;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   if (head_dim == 64) {
     using C = AttnCfg<64>;
     if (static_cast<int64_t>(C::kSmemBytes) > info.max_smem_optin)
       return ko::fail(KO_ERR_UNSUPPORTED, std::string(who) + ": not enough shared memory on this device");
-    cudaError_t e = cudaFuncSetAttribute(attention_tf32x3_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(C::kSmemBytes));
+    e = cudaFuncSetAttribute(attention_tf32x3_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(C::kSmemBytes));
     if (e != cudaSuccess) return ko::fail(static_cast<int>(e), std::string(who) + ": cudaFuncSetAttribute failed");
-    attention_tf32x3_kernel<64><<<grid, kThreads, C::kSmemBytes, st>>>(mq, mk, a);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    e = cudaLaunchKernelEx(&cfg, attention_tf32x3_kernel<64>, mq, mk, a);
   } else {
     using C = AttnCfg<32>;
-    cudaError_t e = cudaFuncSetAttribute(attention_tf32x3_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(C::kSmemBytes));
+    e = cudaFuncSetAttribute(attention_tf32x3_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(C::kSmemBytes));
     if (e != cudaSuccess) return ko::fail(static_cast<int>(e), std::string(who) + ": cudaFuncSetAttribute failed");
-    attention_tf32x3_kernel<32><<<grid, kThreads, C::kSmemBytes, st>>>(mq, mk, a);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    e = cudaLaunchKernelEx(&cfg, attention_tf32x3_kernel<32>, mq, mk, a);
   }
+  if (e != cudaSuccess) return ko::fail(static_cast<int>(e), std::string(who) + ": launch failed");
   return ko::check_launch(who);
 }

@@ -31,9 +31,11 @@
 //   warps 5-12  loaders: the q tile and this CTA's half of the first k tile arrive by TMA and are split in place,
 //               q by warps 9-12 and k by warps 5-8 at the same time; later key blocks stream from global memory
 //               (128-bit loads; warps 5-8 stream this CTA's k rows, 9-12 its v columns, each holding the next
-//               half tile in registers), split into hi / lo and written into one of two shared-memory buffers in
-//               the MMA's 128-byte-swizzled K-major layout. v is written transposed (head dim x keys), the K-major
-//               form of the P.V product's B operand.
+//               half tile in registers), split into hi / lo and written into one of two shared-memory buffers
+//               with 128-bit stores: k in the S MMA's 128-byte-swizzled K-major layout; v (head dim 64) as it is,
+//               keys x this CTA's 32 head-dim columns, which the P.V MMA reads as an MN-major B operand (head dim
+//               32 leaves a CTA 16 columns, less than one MN-major row: that v is written transposed, head dim x
+//               keys, the K-major form).
 // A query tile count that is odd gets one more tile of padding rows (zero queries, never stored).
 // Tensor memory (512 columns per CTA): two S / P_hi buffers [0,256), P_lo [256,384), two O_j buffers of HD columns
 // from 384. With two S buffers the tensor cores compute S_{j+1} while the softmax warps work on block j, and
@@ -141,6 +143,21 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const bool ok = mbar_wait(bar, parity, abort);
   return __all_sync(0xffffffffu, ok);
+}
+
+// Shared-memory descriptor of an MN-major tf32 operand tile: 128-byte rows of the M / N dimension (32 values), 4-row
+// atoms along K 512 bytes apart, the 32-byte chunks of a row permuted by chunk ^ (row & 3) (for 32-bit types the
+// MN-major form takes this 128-byte swizzle with 32-byte atoms, layout type 1), atoms on 512-byte boundaries.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128_32b(uint32_t addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);         // start address
+  // leading byte offset: the next 32 columns. A CTA's half has one 32-column group, so it is never used, but it
+  // must be a real offset: 16 bytes here made the MMA fault with a misaligned address.
+  d |= static_cast<uint64_t>((16384u >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((512u >> 4) & 0x3FFFu) << 32;   // stride byte offset: next 4 rows of K
+  d |= static_cast<uint64_t>(1u) << 46;                       // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(1u) << 61;                       // layout: 128-byte swizzle, 32-byte atoms
+  return d;
 }
 
 // tcgen05 of a CTA pair (cta_group::2): every tcgen05 operation of the kernel names the pair. The allocation is made
@@ -291,7 +308,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
       // and receiving its 128 rows of the product in its own tensor memory.
       // The whole warp runs this loop with the same values in every lane; one elected lane issues each MMA.
       const uint32_t sb = smem_addr(smem);
-      constexpr uint32_t idesc_o = idesc_tf32(2 * BQ, HD);
+      // head dim 64: each CTA's v half (32 columns) is one 128-byte MN-major column group; bit 16 = B MN-major
+      constexpr bool kVMN = HD == 64;
+      constexpr uint32_t idesc_o = idesc_tf32(2 * BQ, HD) | (kVMN ? (1u << 16) : 0u);
       const uint64_t dq_hi = smem_desc_k_sw128(sb), dq_lo = smem_desc_k_sw128(sb + C::kOffQlo);
       auto issue_s = [&](int j) {  // S_j = Q K_j^T into S buffer j & 1
         const uint32_t d = tmem + kColS + static_cast<uint32_t>(j & 1) * BKEY;
@@ -331,7 +350,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
         const uint32_t d = tmem + kColO + static_cast<uint32_t>(j & 1) * HD;
         const uint32_t p_hi = tmem + kColS + static_cast<uint32_t>(j & 1) * BKEY;
         const uint32_t vb0 = sb + C::kOffV + static_cast<uint32_t>(j & 1) * C::kVBufBytes;
-        const uint64_t dv_hi = smem_desc_k_sw128(vb0), dv_lo = smem_desc_k_sw128(vb0 + C::kVBytes);
+        const uint64_t dv_hi = kVMN ? smem_desc_mn_sw128_32b(vb0) : smem_desc_k_sw128(vb0);
+        const uint64_t dv_lo = kVMN ? smem_desc_mn_sw128_32b(vb0 + C::kVBytes) : smem_desc_k_sw128(vb0 + C::kVBytes);
+        // k-step kk (8 keys): MN-major, 8 rows of 128 bytes; K-major, 32 bytes within a 32-key row block
+        auto voff = [&](int kk) {
+          return static_cast<uint64_t>(kVMN ? kk * 64 : ((kk >> 2) * (HD / 2 * 128) + (kk & 3) * 32) >> 4);
+        };
         const int ksteps = (keys_of(j) + 7) >> 3;
         // The P_lo products first, then a commit that hands the P_lo columns back to the softmax warps: they
         // write P_{j+1} while the P_hi products of this block (two thirds of its MMAs) still run. A full block's
@@ -340,26 +364,26 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
         if (ksteps == BKEY / 8) {
 #pragma unroll
           for (int kk = 0; kk < BKEY / 8; ++kk) {  // 8 keys per k-step
-            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD / 2 * 128) + (kk & 3) * 32) >> 4);
+            const uint64_t off = voff(kk);
             mma_pair_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
           }
           mma_commit_pair_w(plo_free);
 #pragma unroll
           for (int kk = 0; kk < BKEY / 8; ++kk) {
-            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD / 2 * 128) + (kk & 3) * 32) >> 4);
+            const uint64_t off = voff(kk);
             mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_lo + off, idesc_o, 1u);
             mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + off, idesc_o, 1u);
           }
         } else {  // a short last block
 #pragma unroll 1
           for (int kk = 0; kk < ksteps; ++kk) {
-            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD / 2 * 128) + (kk & 3) * 32) >> 4);
+            const uint64_t off = voff(kk);
             mma_pair_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
           }
           mma_commit_pair_w(plo_free);
 #pragma unroll 1
           for (int kk = 0; kk < ksteps; ++kk) {
-            const uint64_t off = static_cast<uint64_t>(((kk >> 2) * (HD / 2 * 128) + (kk & 3) * 32) >> 4);
+            const uint64_t off = voff(kk);
             mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_lo + off, idesc_o, 1u);
             mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + off, idesc_o, 1u);
           }
@@ -573,17 +597,30 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
         if (j >= 2 && !mbar_wait(&o_full[j & 1], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag)) break;
         const uint32_t vbuf = C::kOffV + static_cast<uint32_t>(j & 1) * C::kVBufBytes;
         const int key = g;
-        const uint32_t base = (key >> 5) * (HD / 2 * 128) + ((key & 3) << 2);
+        if constexpr (HD == 64) {
+          // as it is: row `key` of 128 bytes, its 16-byte chunk i at (i ^ ((key & 3) << 1)), 128-bit stores
 #pragma unroll
-        for (int i = 0; i < kTileChunks; ++i) {
-          const float* src = reinterpret_cast<const float*>(&reg[i]);
+          for (int i = 0; i < kTileChunks; ++i) {
+            const uint32_t off = key * 128 + ((i ^ ((key & 3) << 1)) << 4);
+            // v itself as hi (read truncated to tf32) and its tail as lo: P.V errors are not amplified
+            const float4 lo = make_float4(tf32_tail(reg[i].x), tf32_tail(reg[i].y), tf32_tail(reg[i].z),
+                                          tf32_tail(reg[i].w));
+            *reinterpret_cast<float4*>(smem + vbuf + off) = reg[i];
+            *reinterpret_cast<float4*>(smem + vbuf + C::kVBytes + off) = lo;
+          }
+        } else {
+          const uint32_t base = (key >> 5) * (HD / 2 * 128) + ((key & 3) << 2);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int d = 4 * i + e;  // head-dim column within this CTA's half
-            const uint32_t off = base + sw128(d, (key & 31) >> 2);
-            const float hi = src[e], lo = tf32_tail(src[e]);  // v itself as hi: P.V errors are not amplified
-            *reinterpret_cast<float*>(smem + vbuf + off) = hi;
-            *reinterpret_cast<float*>(smem + vbuf + C::kVBytes + off) = lo;
+          for (int i = 0; i < kTileChunks; ++i) {
+            const float* src = reinterpret_cast<const float*>(&reg[i]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int d = 4 * i + e;  // head-dim column within this CTA's half
+              const uint32_t off = base + sw128(d, (key & 31) >> 2);
+              const float hi = src[e], lo = tf32_tail(src[e]);  // v itself as hi: P.V errors are not amplified
+              *reinterpret_cast<float*>(smem + vbuf + off) = hi;
+              *reinterpret_cast<float*>(smem + vbuf + C::kVBytes + off) = lo;
+            }
           }
         }
         fence_proxy_async_smem();

@@ -15,11 +15,13 @@
 // key block's P.V product lands in a fresh tensor-memory accumulator and is added into the fp32 output row in
 // registers, so the long sum over keys is a plain fp32 register sum, not a tensor-core accumulation.
 //
-// Kernel structure: a pair of CTAs (a cluster of two on one GPU) per (two 128-query tiles, head, batch item); 13
-// warps each. The pair runs the 5th-generation tensor cores of two SMs as one (tcgen05 cta_group::2): every MMA
-// has M = 256, rows 0-127 being the leader's (rank 0) query tile and 128-255 the peer's, each CTA holding its own
-// A rows and HALF of B at the same shared-memory offset and receiving its 128 rows of the product in its own tensor
-// memory. So each SM loads, splits and stores only half of each k / v tile, and its tensor core reads only half of
+// Kernel structure: pairs of CTAs (clusters of two on one GPU), as many as the GPU holds at once, 13 warps each;
+// each pair loops over work items (two 128-query tiles, head, batch item), the key blocks of all its items forming
+// one pipeline: the next item's q tile loads while the current item's last blocks run, so a short sequence (a
+// 401-token window: four key blocks) does not pay a whole CTA prologue per item. The pair runs the 5th-generation
+// tensor cores of two SMs as one (tcgen05 cta_group::2): every MMA has M = 256, rows 0-127 being the leader's
+// (rank 0) query tile and 128-255 the peer's, each CTA holding its own A rows and HALF of B at the same
+// shared-memory offset and receiving its 128 rows of the product in its own tensor memory. So each SM loads, splits and stores only half of each k / v tile, and its tensor core reads only half of
 // each B operand; and the halves fit twice in shared memory, so the loaders write block j + 1 while block j's
 // MMAs read block j (with one buffer, each block's k and v writes waited for the previous block's MMAs).
 //   warp 0      allocates the pair's tensor memory; in the leader, one lane issues the MMAs of both CTAs:
@@ -28,10 +30,10 @@
 //   warps 1-4   softmax + output: one thread per query row. Reads S from tensor memory, updates the row's running
 //               max / sum, writes P (hi and lo) back into tensor memory for the P.V MMA, then adds O_j into the
 //               output row it keeps in registers. At the end divides by the sum and stores the row.
-//   warps 5-12  loaders: the q tile and this CTA's half of the first k tile arrive by TMA and are split in place,
-//               q by warps 9-12 and k by warps 5-8 at the same time; later key blocks stream from global memory
-//               (128-bit loads; warps 5-8 stream this CTA's k rows, 9-12 its v columns, each holding the next
-//               half tile in registers), split into hi / lo and written into one of two shared-memory buffers
+//   warps 5-12  loaders: per item, warps 9-12 load the q tile by TMA once the previous item's last S MMA has read
+//               the q buffer, and split it in place; key blocks stream from global memory (128-bit loads; warps
+//               5-8 stream this CTA's k rows, 9-12 its v columns, each holding the next half tile, of the same
+//               item or the next, in registers), split into hi / lo and written into one of two shared-memory buffers
 //               with 128-bit stores: k in the S MMA's 128-byte-swizzled K-major layout; v (head dim 64) as it is,
 //               keys x this CTA's 32 head-dim columns, which the P.V MMA reads as an MN-major B operand (head dim
 //               32 leaves a CTA 16 columns, less than one MN-major row: that v is written transposed, head dim x
@@ -74,6 +76,8 @@ struct AttnArgs {
   int64_t q_bstride, k_bstride, v_bstride, o_bstride;  // elements between consecutive batch items
   int q_row, k_row, v_row, o_row;                      // elements between consecutive tokens
   int L, n_kblocks;
+  int heads, pairs;              // query-tile pairs per sequence (an odd tile count gets a padding tile)
+  int total_items, n_clusters;   // work items (pair, head, batch item) and the CTA pairs that share them
   float scale_log2;  // softmax scale * log2(e): exponentials are taken as exp2
   int* dev_status;
 };
@@ -92,7 +96,8 @@ struct AttnCfg {
   static constexpr uint32_t kOffBars = kOffV + 2 * kVBufBytes;
   // At least 120 KB even where the tiles need less (head dim 32), so that one CTA per SM holds all 512 tensor-
   // memory columns and no second CTA waits in tcgen05.alloc.
-  static constexpr size_t kSmemNeed = 1024 + kOffBars + 256;
+  static constexpr uint32_t kOffRowPtr = kOffBars + 256;  // [BQ] output-row pointers of the softmax threads
+  static constexpr size_t kSmemNeed = 1024 + kOffRowPtr + BQ * 8;
   static constexpr size_t kSmemBytes = kSmemNeed > 120 * 1024 ? kSmemNeed : 120 * 1024;
   static_assert(HD == 32 || HD == 64, "head dim 32 or 64");
 };
@@ -221,33 +226,44 @@ __device__ __forceinline__ float fast_exp2(float x) {
 
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __grid_constant__ CUtensorMap map_q,
-                                                                        const __grid_constant__ CUtensorMap map_k,
                                                                         const AttnArgs a) {
   using C = AttnCfg<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
   // Barriers the leader's MMA warp waits on collect arrivals from both CTAs of the pair; the MMA commits arrive on
-  // the same barrier in both CTAs (multicast).
+  // the same barrier in both CTAs (multicast). Block phases run over the pair's whole sequence of key blocks
+  // (g = item * nkb + j), so the pipeline continues from one work item into the next.
   uint64_t* q_ready = bars + 0;   // q tile split            (4 v-loader warps x 2 CTAs, leader)
   uint64_t* k_full = bars + 1;    // k half tile written, x2 (4 k-loader warps x 2 CTAs, leader)
   uint64_t* v_full = bars + 3;    // v half tile written, x2 (4 v-loader warps x 2 CTAs, leader)
-  uint64_t* s_full = bars + 5;    // S_j complete, x2        (1 commit, both CTAs)
-  uint64_t* p_full = bars + 7;    // P_j written             (4 softmax warps x 2 CTAs, leader)
-  uint64_t* o_full = bars + 8;    // O_j complete, x2        (1 commit, both CTAs)
+  uint64_t* s_full = bars + 5;    // S_g complete, x2        (1 commit, both CTAs)
+  uint64_t* p_full = bars + 7;    // P_g written             (4 softmax warps x 2 CTAs, leader)
+  uint64_t* o_full = bars + 8;    // O_g complete, x2        (1 commit, both CTAs)
   uint64_t* mma_done = bars + 12;  // every MMA complete      (1 commit, both CTAs)
-  uint64_t* plo_free = bars + 13;  // P_j.V_j's P_lo products done (1 commit, both CTAs)
+  uint64_t* plo_free = bars + 13;  // P_g.V_g's P_lo products done (1 commit, both CTAs)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   uint64_t* q_tma = bars + 15;     // q tile landed (fp32)     (1 arrival + tx bytes)
-  uint64_t* k0_tma = bars + 16;    // first k half tile landed (1 arrival + tx bytes)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * BQ;
   const uint32_t rank = cluster_ctarank();  // 0: the leader, which issues the pair's MMAs
   const int nkb = a.n_kblocks;
-  // keys of block j, the S MMA's N (keys rounded up to 16) and this CTA's share of the block's k rows (N / 2,
-  // starting at rank * N / 2)
+  // Work items (query-tile pair, head, batch item), the pair index fastest so that concurrent pairs share k / v
+  // in L2; this pair takes items cluster, cluster + n_clusters, ...
+  const int cluster = static_cast<int>(blockIdx.x >> 1);
+  const int n_items = cluster < a.total_items ? (a.total_items - cluster + a.n_clusters - 1) / a.n_clusters : 0;
+  const int n_blocks = n_items * nkb;  // key blocks of all this pair's items, in order
+  struct Item {
+    int b, h, q0;
+  };
+  auto item_of = [&](int k) -> Item {
+    const int it = cluster + k * a.n_clusters;
+    const int pr = it % a.pairs, rest = it / a.pairs;
+    return Item{rest / a.heads, rest % a.heads, (2 * pr + static_cast<int>(rank)) * BQ};
+  };
+  // keys of block j of an item, the S MMA's N (keys rounded up to 16) and this CTA's share of the block's k rows
+  // (N / 2, starting at rank * N / 2)
   auto keys_of = [&](int j) { return min(BKEY, a.L - j * BKEY); };
   auto n_of = [&](int j) { return (keys_of(j) + 15) & ~15; };
   // Arrive on the leader's copy of a barrier (this CTA's own when it is the leader): the leader's barrier area is
@@ -273,20 +289,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
     mbar_init(mma_done, 1);
     mbar_init(plo_free, 1);
     mbar_init(q_tma, 1);
-    mbar_init(k0_tma, 1);
     *abort_flag = 0;
     fence_barrier_init();
-    // The q tile and this CTA's half of the first k tile come in by TMA at once (fp32, in the 128-byte-swizzled
-    // K-major layout the MMAs read, one 32-column box per 128-byte k-block); the loaders split them in place.
-    const int bq = a.q_bstride ? b : 0, bk = a.k_bstride ? b : 0;
-    mbar_arrive_expect_tx(q_tma, C::kQBytes);
-    mbar_arrive_expect_tx(k0_tma, C::kKBytes);
-    const int k0_row = static_cast<int>(rank) * (n_of(0) / 2);
-#pragma unroll
-    for (int kb = 0; kb < C::kKB; ++kb) {
-      tma_load_3d(&map_q, q_tma, smem + kb * (BQ * 128), h * HD + kb * 32, q0, bq);
-      tma_load_3d(&map_k, k0_tma, smem + C::kOffK + kb * (KHALF * 128), h * HD + kb * 32, k0_row, bk);
-    }
   }
   if (warp == 0) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -299,23 +303,25 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (rank == 0) {
+    if (rank == 0 && n_blocks > 0) {
       // ---------------- MMA issuer (leader) ----------------
-      // Order on the tensor pipes of the pair: S_0, then per block j: S_{j+1} (into the other S buffer,
-      // overlapping softmax_j), P_j.V_j. S_{j+1} reuses the buffer of P_{j-1}, so it waits for P_{j-1}.V_{j-1}.
+      // Order on the tensor pipes of the pair: S_0, then per block g: S_{g+1} (into the other S buffer,
+      // overlapping softmax_g), P_g.V_g. S_{g+1} reuses the buffer of P_{g-1}, so it waits for P_{g-1}.V_{g-1}.
       // Each MMA has M = 256: rows 0-127 are the leader's query tile, 128-255 the peer's, each CTA holding its A
       // rows (q, or P in its tensor memory) and half of B (k rows, or v columns) at the same shared-memory offset,
-      // and receiving its 128 rows of the product in its own tensor memory.
+      // and receiving its 128 rows of the product in its own tensor memory. The first S of an item waits for its
+      // q tile, which the loaders write once the previous item's last S is complete.
       // The whole warp runs this loop with the same values in every lane; one elected lane issues each MMA.
       const uint32_t sb = smem_addr(smem);
       // head dim 64: each CTA's v half (32 columns) is one 128-byte MN-major column group; bit 16 = B MN-major
       constexpr bool kVMN = HD == 64;
       constexpr uint32_t idesc_o = idesc_tf32(2 * BQ, HD) | (kVMN ? (1u << 16) : 0u);
       const uint64_t dq_hi = smem_desc_k_sw128(sb), dq_lo = smem_desc_k_sw128(sb + C::kOffQlo);
-      auto issue_s = [&](int j) {  // S_j = Q K_j^T into S buffer j & 1
-        const uint32_t d = tmem + kColS + static_cast<uint32_t>(j & 1) * BKEY;
+      auto issue_s = [&](int g) {  // S_g = Q K_g^T into S buffer g & 1
+        const int j = g % nkb;
+        const uint32_t d = tmem + kColS + static_cast<uint32_t>(g & 1) * BKEY;
         const uint32_t idesc_s = idesc_tf32(2 * BQ, n_of(j));
-        const uint32_t kb0 = sb + C::kOffK + static_cast<uint32_t>(j & 1) * C::kKBufBytes;
+        const uint32_t kb0 = sb + C::kOffK + static_cast<uint32_t>(g & 1) * C::kKBufBytes;
         const uint64_t dk_hi = smem_desc_k_sw128(kb0), dk_lo = smem_desc_k_sw128(kb0 + C::kKBytes);
 #pragma unroll
         for (int s = 0; s < C::kKB * 4; ++s) {  // 8-wide k-steps over the head dimension
@@ -325,84 +331,89 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
           mma_pair_tf32_w(d, dq_hi + qoff, dk_lo + koff, idesc_s, 1u);
           mma_pair_tf32_w(d, dq_hi + qoff, dk_hi + koff, idesc_s, 1u);
         }
-        mma_commit_pair_w(&s_full[j & 1]);  // the k loaders wait on it too (S_j done = k buffer j & 1 free)
+        mma_commit_pair_w(&s_full[g & 1]);  // the loaders wait on it too (S_g done = k buffer g & 1 free)
       };
-      bool ok = warp_wait(q_ready, 0, abort_flag) && warp_wait(&k_full[0], 0, abort_flag);
+      // block g may issue its S once its item's q tile is split and its k half tile written
+      auto s_ready = [&](int g) -> bool {
+        if (g % nkb == 0 && !warp_wait(q_ready, static_cast<uint32_t>(g / nkb) & 1u, abort_flag)) return false;
+        return warp_wait(&k_full[g & 1], static_cast<uint32_t>(g >> 1) & 1u, abort_flag);
+      };
+      bool ok = s_ready(0);
       if (ok) {
         tc_fence_after();
         issue_s(0);
       }
-      for (int j = 0; j < nkb && ok; ++j) {
-        if (j + 1 < nkb) {
-          const uint32_t kpar = static_cast<uint32_t>((j + 1) >> 1) & 1u;
-          const uint32_t opar = static_cast<uint32_t>((j - 1) >> 1) & 1u;
-          if (!warp_wait(&k_full[(j + 1) & 1], kpar, abort_flag)) break;
-          if (j >= 1 && !warp_wait(&o_full[(j - 1) & 1], opar, abort_flag)) break;
-          tc_fence_after();
-          issue_s(j + 1);
-        }
-        // O_j = P_j V_j into O buffer j & 1, once P_j is written and V_j landed. The buffer held O_{j-2}, which
-        // every softmax warp read (add_block(j - 2)) before it wrote P_j: p_full covers it.
-        if (!warp_wait(p_full, static_cast<uint32_t>(j) & 1u, abort_flag) ||
-            !warp_wait(&v_full[j & 1], static_cast<uint32_t>(j >> 1) & 1u, abort_flag))
+      // S_{g+1} (buffer (g + 1) & 1 held P_{g-1}: P_{g-1}.V_{g-1} must be complete)
+      auto next_s = [&](int g) -> bool {
+        if (!s_ready(g + 1)) return false;
+        if (g >= 1 && !warp_wait(&o_full[(g - 1) & 1], static_cast<uint32_t>((g - 1) >> 1) & 1u, abort_flag))
+          return false;
+        tc_fence_after();
+        issue_s(g + 1);
+        return true;
+      };
+      for (int g = 0; g < n_blocks && ok; ++g) {
+        if (g + 1 < n_blocks && !next_s(g)) break;
+        // O_g = P_g V_g into O buffer g & 1, once P_g is written and V_g landed. The buffer held O_{g-2}, which
+        // every softmax warp read (add_block(g - 2)) before it wrote P_g: p_full covers it.
+        if (!warp_wait(p_full, static_cast<uint32_t>(g) & 1u, abort_flag) ||
+            !warp_wait(&v_full[g & 1], static_cast<uint32_t>(g >> 1) & 1u, abort_flag))
           break;
         tc_fence_after();
-        const uint32_t d = tmem + kColO + static_cast<uint32_t>(j & 1) * HD;
-        const uint32_t p_hi = tmem + kColS + static_cast<uint32_t>(j & 1) * BKEY;
-        const uint32_t vb0 = sb + C::kOffV + static_cast<uint32_t>(j & 1) * C::kVBufBytes;
+        const uint32_t d = tmem + kColO + static_cast<uint32_t>(g & 1) * HD;
+        const uint32_t p_hi = tmem + kColS + static_cast<uint32_t>(g & 1) * BKEY;
+        const uint32_t vb0 = sb + C::kOffV + static_cast<uint32_t>(g & 1) * C::kVBufBytes;
         const uint64_t dv_hi = kVMN ? smem_desc_mn_sw128_32b(vb0) : smem_desc_k_sw128(vb0);
         const uint64_t dv_lo = kVMN ? smem_desc_mn_sw128_32b(vb0 + C::kVBytes) : smem_desc_k_sw128(vb0 + C::kVBytes);
         // k-step kk (8 keys): MN-major, 8 rows of 128 bytes; K-major, 32 bytes within a 32-key row block
         auto voff = [&](int kk) {
           return static_cast<uint64_t>(kVMN ? kk * 64 : ((kk >> 2) * (HD / 2 * 128) + (kk & 3) * 32) >> 4);
         };
-        const int ksteps = (keys_of(j) + 7) >> 3;
+        const int ksteps = (keys_of(g % nkb) + 7) >> 3;
         // The P_lo products first, then a commit that hands the P_lo columns back to the softmax warps: they
-        // write P_{j+1} while the P_hi products of this block (two thirds of its MMAs) still run. A full block's
+        // write P_{g+1} while the P_hi products of this block (two thirds of its MMAs) still run. A full block's
         // MMAs are issued from fully unrolled code (a rolled loop's address arithmetic would make the issue, not
         // the pipe, the limit).
         if (ksteps == BKEY / 8) {
 #pragma unroll
           for (int kk = 0; kk < BKEY / 8; ++kk) {  // 8 keys per k-step
-            const uint64_t off = voff(kk);
-            mma_pair_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
+            mma_pair_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + voff(kk), idesc_o, kk == 0 ? 0u : 1u);
           }
           mma_commit_pair_w(plo_free);
 #pragma unroll
           for (int kk = 0; kk < BKEY / 8; ++kk) {
-            const uint64_t off = voff(kk);
-            mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_lo + off, idesc_o, 1u);
-            mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + off, idesc_o, 1u);
+            mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_lo + voff(kk), idesc_o, 1u);
+            mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + voff(kk), idesc_o, 1u);
           }
         } else {  // a short last block
 #pragma unroll 1
           for (int kk = 0; kk < ksteps; ++kk) {
-            const uint64_t off = voff(kk);
-            mma_pair_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + off, idesc_o, kk == 0 ? 0u : 1u);
+            mma_pair_tf32_ts_w(d, tmem + kColPlo + 8 * kk, dv_hi + voff(kk), idesc_o, kk == 0 ? 0u : 1u);
           }
           mma_commit_pair_w(plo_free);
 #pragma unroll 1
           for (int kk = 0; kk < ksteps; ++kk) {
-            const uint64_t off = voff(kk);
-            mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_lo + off, idesc_o, 1u);
-            mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + off, idesc_o, 1u);
+            mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_lo + voff(kk), idesc_o, 1u);
+            mma_pair_tf32_ts_w(d, p_hi + 8 * kk, dv_hi + voff(kk), idesc_o, 1u);
           }
         }
-        // One commit per event: the v loaders wait on o_full as well (P_j.V_j done = v buffer j & 1 free).
-        mma_commit_pair_w(&o_full[j & 1]);
+        // One commit per event: the v loaders wait on o_full as well (P_g.V_g done = v buffer g & 1 free).
+        mma_commit_pair_w(&o_full[g & 1]);
       }
-      // Drain: every MMA this warp issued completes before either CTA releases its tensor memory.
-      mma_commit_pair_w(mma_done);
     }
+    // Drain: every MMA the leader issued completes before either CTA releases its tensor memory.
+    if (rank == 0) mma_commit_pair_w(mma_done);
     volatile int never = 0;
     if (!warp_wait(mma_done, 0, &never)) *abort_flag = 1;
   } else if (warp < kLoadWarp0) {
     // ---------------- softmax + output, one thread per query row ----------------
-    // Block j, two passes over S_j in tensor memory: the first finds the row maximum, which sets the block's
-    // offset m = max(m, block maximum) (online softmax, P <= 1); once P_{j-1}.V_{j-1}'s P_lo products are done
-    // (the P_lo columns are free) the second turns each 16-key chunk into P = exp2(S * c - m), written as P
-    // itself and its tf32 tail. The max pass overlaps that wait. Then, once all of P_{j-1}.V_{j-1} is complete,
-    // o = o * alpha + that block's product.
+    // Block g (key block j of item g / nkb), two passes over S_g in tensor memory: the first finds the row
+    // maximum, which sets the block's offset m = max(m, block maximum) (online softmax, P <= 1); once
+    // P_{g-1}.V_{g-1}'s P_lo products are done (the P_lo columns are free) the second turns each 16-key chunk
+    // into P = exp2(S * c - m), written as P itself and its tf32 tail. The max pass overlaps that wait. Then,
+    // once all of P_{g-1}.V_{g-1} is complete, o = o * alpha + that block's product. An item's first block starts
+    // from m = -inf, so its alpha is 0 and the fold of its first product replaces o; the previous item's row is
+    // finished (its last fold, the division by its sum and the store) just before that.
     const int quad = warp & 3;  // tensor-memory lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
@@ -411,10 +422,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
     for (int d = 0; d < HD; ++d) o[d] = 0.f;
     float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
     bool ok = true;
-    auto add_block = [&](int jb, float alpha) -> bool {  // o = o * alpha + O_jb
-      if (!warp_wait(&o_full[jb & 1], static_cast<uint32_t>(jb >> 1) & 1u, abort_flag)) return false;
+    auto add_block = [&](int gb, float alpha) -> bool {  // o = o * alpha + O_gb
+      if (!warp_wait(&o_full[gb & 1], static_cast<uint32_t>(gb >> 1) & 1u, abort_flag)) return false;
       tc_fence_after();
-      const uint32_t ob = trow + kColO + static_cast<uint32_t>(jb & 1) * HD;
+      const uint32_t ob = trow + kColO + static_cast<uint32_t>(gb & 1) * HD;
 #pragma unroll
       for (int c = 0; c < HD / 16; ++c) {
         uint32_t r[16];
@@ -425,13 +436,33 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
       }
       return true;
     };
-    for (int j = 0; j < nkb; ++j) {
-      if (!warp_wait(&s_full[j & 1], static_cast<uint32_t>(j >> 1) & 1u, abort_flag)) {
+    // This thread's output row of item k (null for a padding row), and the store of the finished row.
+    auto row_ptr = [&](int k) -> float4* {
+      const Item itm = item_of(k);
+      const int qi = itm.q0 + row;
+      if (qi >= a.L) return nullptr;
+      return reinterpret_cast<float4*>(a.o + static_cast<int64_t>(itm.b) * a.o_bstride +
+                                       static_cast<int64_t>(qi) * a.o_row + itm.h * HD);
+    };
+    auto store_row = [&](float4* dst, float l_row) {
+      if (dst == nullptr) return;
+      const float inv = 1.0f / l_row;
+#pragma unroll
+      for (int d = 0; d < HD / 4; ++d)
+        dst[d] = make_float4(o[4 * d] * inv, o[4 * d + 1] * inv, o[4 * d + 2] * inv, o[4 * d + 3] * inv);
+    };
+    // the current item's row pointer waits in shared memory (in registers it pushed the loop over its budget)
+    float4** orow = reinterpret_cast<float4**>(smem + C::kOffRowPtr) + row;
+    *orow = n_blocks > 0 ? row_ptr(0) : nullptr;
+    for (int g = 0; g < n_blocks; ++g) {
+      const int j = g % nkb;
+      if (j == 0) m = -INFINITY;  // a new item: its first block's alpha is 0, which also restarts the sum
+      if (!warp_wait(&s_full[g & 1], static_cast<uint32_t>(g >> 1) & 1u, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t srow = trow + kColS + static_cast<uint32_t>(j & 1) * BKEY;
+      const uint32_t srow = trow + kColS + static_cast<uint32_t>(g & 1) * BKEY;
       const uint32_t plrow = trow + kColPlo;
       const int valid = keys_of(j);
       const int chunks = (valid + 15) >> 4;  // 16-column chunks that hold keys of this block
@@ -454,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
         mx = fmax3(mx, fmax3(m0, m1, m2), fmax3(m3, m4, f[15]));
       }
       const float mb = fmaxf(m, mx * a.scale_log2);  // offset of this block's P
-      if (j >= 1 && !warp_wait(plo_free, static_cast<uint32_t>(j - 1) & 1u, abort_flag)) {
+      if (g >= 1 && !warp_wait(plo_free, static_cast<uint32_t>(g - 1) & 1u, abort_flag)) {
         ok = false;
         break;
       }
@@ -480,85 +511,64 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
       }
       const float ls = ls0 + ls1;
       tmem_st_wait();
-      const float alpha = fast_exp2(m - mb);  // 0 for the first block (m = -inf)
+      const float alpha = fast_exp2(m - mb);  // 0 for an item's first block (m = -inf)
+      const float l_done = l;                 // the previous item's sum when j == 0 (stored below)
       l = l * alpha + ls;
       m = mb;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) arrive_leader(p_full);
-      if (j >= 1 && !add_block(j - 1, alpha_prev)) {
-        ok = false;
-        break;
+      if (g >= 1) {
+        if (!add_block(g - 1, alpha_prev)) {
+          ok = false;
+          break;
+        }
+        if (j == 0) {  // block g - 1 was the previous item's last: finish its row, start the next from zero
+          store_row(*orow, l_done);
+          *orow = row_ptr(g / nkb);
+#pragma unroll
+          for (int d = 0; d < HD; ++d) o[d] = 0.f;
+        }
       }
       alpha_prev = alpha;
     }
-    if (ok && !add_block(nkb - 1, alpha_prev)) ok = false;
-    const int qi = q0 + row;
-    if (ok && qi < a.L) {
-      const float inv = 1.0f / l;
-      float4* dst = reinterpret_cast<float4*>(a.o + static_cast<int64_t>(b) * a.o_bstride +
-                                              static_cast<int64_t>(qi) * a.o_row + h * HD);
-#pragma unroll
-      for (int d = 0; d < HD / 4; ++d)
-        dst[d] = make_float4(o[4 * d] * inv, o[4 * d + 1] * inv, o[4 * d + 2] * inv, o[4 * d + 3] * inv);
-    }
+    if (ok && n_blocks > 0 && add_block(n_blocks - 1, alpha_prev)) store_row(*orow, l);
   } else {
     // ---------------- loaders ----------------
-    // The q tile and this CTA's half of the first k tile come by TMA; the v group (warps 9-12) splits q in place
-    // while the k group (warps 5-8) splits the k half, so S_0 waits for one split, not two in a row. Then warps
-    // 5-8 stream this CTA's k halves (its N / 2 keys of each block) and warps 9-12 its v halves (all keys of a
-    // block, head-dim columns [rank * HD / 2, (rank + 1) * HD / 2)), into alternating buffers, each group holding
-    // its next half tile in registers while the current one is written.
+    // Per item the v group (warps 9-12) loads the q tile by TMA, once the previous item's last S MMA has read the
+    // q buffer, and splits it in place. Warps 5-8 stream this CTA's k halves (its N / 2 keys of each block) and
+    // warps 9-12 its v halves (all keys of a block, head-dim columns [rank * HD / 2, (rank + 1) * HD / 2)), into
+    // alternating buffers, each group holding its next half tile (of the same item or the next) in registers
+    // while the current one is written.
     const int t = threadIdx.x - kLoadWarp0 * 32;  // 0..255
     constexpr int Q4 = HD / 4;                   // float4 per q / k row
-    // hi in place, lo at the same offset in the lo buffer (the split is elementwise: any cover of the tile works)
-    auto split_in_place = [&](uint32_t off_hi, uint32_t off_lo, int n4, int tid, int nthreads) {
-      for (int i = tid; i < n4; i += nthreads) {
-        float4* src = reinterpret_cast<float4*>(smem + off_hi) + i;
-        const float4 v = *src;
-        float4 hi, lo;
-        split_tf32(v.x, hi.x, lo.x);
-        split_tf32(v.y, hi.y, lo.y);
-        split_tf32(v.z, hi.z, lo.z);
-        split_tf32(v.w, hi.w, lo.w);
-        *src = hi;
-        reinterpret_cast<float4*>(smem + off_lo)[i] = lo;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-    };
-    constexpr int kGroup = kLoadThreads / 2;  // 128 threads per group
+    constexpr int kGroup = kLoadThreads / 2;     // 128 threads per group
     constexpr int kTileChunks = KHALF * HD / 4 / kGroup;  // float4 per thread of a half tile (k or v)
-    const int g = t & (kGroup - 1);
+    const int g0 = t & (kGroup - 1);
     float4 reg[kTileChunks];
     if (t < kGroup) {
       // k halves: row-major chunks (a warp reads whole rows), stored K-major with the 128-byte swizzle
-      const float* kbp = a.k + static_cast<int64_t>(b) * a.k_bstride + h * HD;
-      auto load = [&](int j) {
+      auto load = [&](int g) {
+        const Item itm = item_of(g / nkb);
+        const int j = g % nkb;
+        const float* kbp = a.k + static_cast<int64_t>(itm.b) * a.k_bstride + itm.h * HD;
         const int half = n_of(j) / 2, r0 = j * BKEY + static_cast<int>(rank) * half;
 #pragma unroll
         for (int i = 0; i < kTileChunks; ++i) {
-          const int idx = i * kGroup + g, r = idx / Q4, kr = r0 + r, kc = idx % Q4;
+          const int idx = i * kGroup + g0, r = idx / Q4, kr = r0 + r, kc = idx % Q4;
           reg[i] = r < half && kr < a.L
                        ? __ldg(reinterpret_cast<const float4*>(kbp + static_cast<int64_t>(kr) * a.k_row) + kc)
                        : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       };
-      // The first k half is split as soon as it lands (the v group splits q meanwhile); the prefetch of the
-      // next one into registers follows, so that its loads do not compete with the split.
-      bool kok = mbar_wait(k0_tma, 0, abort_flag);
-      if (kok) {
-        split_in_place(C::kOffK, C::kOffK + C::kKBytes, static_cast<int>(C::kKBytes / 16), g, kGroup);
-        if (lane == 0) arrive_leader(&k_full[0]);
-      }
-      if (nkb > 1) load(1);
-      for (int j = 1; j < nkb && kok; ++j) {
-        // k buffer j & 1 held tile j - 2: S_{j-2} must be complete
-        if (j >= 2 && !mbar_wait(&s_full[j & 1], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag)) break;
-        const uint32_t kbuf = C::kOffK + static_cast<uint32_t>(j & 1) * C::kKBufBytes;
+      if (n_blocks > 0) load(0);
+      for (int g = 0; g < n_blocks; ++g) {
+        // k buffer g & 1 held block g - 2: S_{g-2} must be complete
+        if (g >= 2 && !mbar_wait(&s_full[g & 1], static_cast<uint32_t>((g - 2) >> 1) & 1u, abort_flag)) break;
+        const uint32_t kbuf = C::kOffK + static_cast<uint32_t>(g & 1) * C::kKBufBytes;
 #pragma unroll
         for (int i = 0; i < kTileChunks; ++i) {
-          const int idx = i * kGroup + g, r = idx / Q4, c = idx % Q4;
+          const int idx = i * kGroup + g0, r = idx / Q4, c = idx % Q4;
           const uint32_t off = (c >> 3) * (KHALF * 128) + sw128(r, c & 7);
           float4 hi, lo;
           split_tf32(reg[i].x, hi.x, lo.x);
@@ -570,33 +580,57 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) arrive_leader(&k_full[j & 1]);
-        if (j + 1 < nkb) load(j + 1);
+        if (lane == 0) arrive_leader(&k_full[g & 1]);
+        if (g + 1 < n_blocks) load(g + 1);
       }
     } else {
-      // v halves: a thread reads one key's HD / 2 columns of this CTA's half (8 or 4 float4) and writes them
-      // transposed (head dim x keys, K-major, 128-byte swizzle): every scalar store of a warp fills one 128-byte
-      // row (32 consecutive keys of one head-dim column).
-      const float* vbp = a.v + static_cast<int64_t>(b) * a.v_bstride + h * HD + static_cast<int>(rank) * (HD / 2);
-      auto load = [&](int j) {
-        const int vr = j * BKEY + g;
+      // v halves: a thread reads one key's HD / 2 columns of this CTA's half (8 or 4 float4)
+      auto load = [&](int g) {
+        const Item itm = item_of(g / nkb);
+        const int vr = (g % nkb) * BKEY + g0;
+        const float* vbp =
+            a.v + static_cast<int64_t>(itm.b) * a.v_bstride + itm.h * HD + static_cast<int>(rank) * (HD / 2);
 #pragma unroll
         for (int i = 0; i < kTileChunks; ++i)
           reg[i] = vr < a.L ? __ldg(reinterpret_cast<const float4*>(vbp + static_cast<int64_t>(vr) * a.v_row) + i)
                             : make_float4(0.f, 0.f, 0.f, 0.f);  // keys past the end: P is 0 there, v must be finite
       };
-      // q: split in place as soon as it lands
-      bool vok = mbar_wait(q_tma, 0, abort_flag);
-      if (vok) {
-        split_in_place(0, C::kOffQlo, static_cast<int>(C::kQBytes / 16), g, kGroup);
-        if (lane == 0) arrive_leader(q_ready);
-      }
-      load(0);
-      for (int j = 0; j < nkb && vok; ++j) {
-        // v buffer j & 1 held tile j - 2: P_{j-2}.V_{j-2} must be complete
-        if (j >= 2 && !mbar_wait(&o_full[j & 1], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag)) break;
-        const uint32_t vbuf = C::kOffV + static_cast<uint32_t>(j & 1) * C::kVBufBytes;
-        const int key = g;
+      if (n_blocks > 0) load(0);
+      bool vok = true;
+      for (int g = 0; g < n_blocks && vok; ++g) {
+        if (g % nkb == 0) {
+          // q of item g / nkb: the previous item's last S (block g - 1) has read the q buffer
+          const int k = g / nkb;
+          if (g >= 1 && !mbar_wait(&s_full[(g - 1) & 1], static_cast<uint32_t>((g - 1) >> 1) & 1u, abort_flag)) break;
+          if (g0 == 0) {
+            const Item itm = item_of(k);
+            const int bq = a.q_bstride ? itm.b : 0;
+            mbar_arrive_expect_tx(q_tma, C::kQBytes);
+#pragma unroll
+            for (int kb = 0; kb < C::kKB; ++kb)
+              tma_load_3d(&map_q, q_tma, smem + kb * (BQ * 128), itm.h * HD + kb * 32, itm.q0, bq);
+          }
+          if (!mbar_wait(q_tma, static_cast<uint32_t>(k) & 1u, abort_flag)) break;
+          // hi in place, lo at the same offset in the lo buffer (elementwise: any cover of the tile works)
+          for (int i = g0; i < static_cast<int>(C::kQBytes / 16); i += kGroup) {
+            float4* src = reinterpret_cast<float4*>(smem) + i;
+            const float4 v = *src;
+            float4 hi, lo;
+            split_tf32(v.x, hi.x, lo.x);
+            split_tf32(v.y, hi.y, lo.y);
+            split_tf32(v.z, hi.z, lo.z);
+            split_tf32(v.w, hi.w, lo.w);
+            *src = hi;
+            reinterpret_cast<float4*>(smem + C::kOffQlo)[i] = lo;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) arrive_leader(q_ready);
+        }
+        // v buffer g & 1 held block g - 2: P_{g-2}.V_{g-2} must be complete
+        if (g >= 2 && !mbar_wait(&o_full[g & 1], static_cast<uint32_t>((g - 2) >> 1) & 1u, abort_flag)) break;
+        const uint32_t vbuf = C::kOffV + static_cast<uint32_t>(g & 1) * C::kVBufBytes;
+        const int key = g0;
         if constexpr (HD == 64) {
           // as it is: row `key` of 128 bytes, its 16-byte chunk i at (i ^ ((key & 3) << 1)), 128-bit stores
 #pragma unroll
@@ -609,6 +643,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
             *reinterpret_cast<float4*>(smem + vbuf + C::kVBytes + off) = lo;
           }
         } else {
+          // transposed (head dim x keys, K-major, 128-byte swizzle): every scalar store of a warp fills one
+          // 128-byte row (32 consecutive keys of one head-dim column)
           const uint32_t base = (key >> 5) * (HD / 2 * 128) + ((key & 3) << 2);
 #pragma unroll
           for (int i = 0; i < kTileChunks; ++i) {
@@ -625,8 +661,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tf32x3_kernel(const __g
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) arrive_leader(&v_full[j & 1]);
-        if (j + 1 < nkb) load(j + 1);
+        if (lane == 0) arrive_leader(&v_full[g & 1]);
+        if (g + 1 < n_blocks) load(g + 1);
       }
     }
   }
@@ -686,21 +722,22 @@ extern "C" int ko_attention_f32(const float* q, const float* k, const float* v, 
   a.scale_log2 = scale * 1.4426950408889634f;
   a.dev_status = dev_status;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // q and k tiles by TMA: [batch][L][heads * head_dim] with the caller's strides, boxes of 32 columns x 128 rows
-  // (q) and x 64 rows (a CTA's half of a k tile); a stride of 0 between batch items maps every item to plane 0
-  CUtensorMap mq, mk;
+  // q tiles by TMA: [batch][L][heads * head_dim] with the caller's strides, boxes of 32 columns x 128 rows; a
+  // stride of 0 between batch items maps every item to plane 0
+  CUtensorMap mq;
   const uint64_t width = static_cast<uint64_t>(heads * head_dim);
   int rc = ko::make_tmap_3d_f32(&mq, q, q_bstride ? batch : 1, L, width, q_row,
                                 q_bstride ? q_bstride : q_row * L + 4, BQ, 32, CU_TENSOR_MAP_SWIZZLE_128B,
                                 "ko_attention_f32 q");
   if (rc) return rc;
-  rc = ko::make_tmap_3d_f32(&mk, k, k_bstride ? batch : 1, L, width, k_row, k_bstride ? k_bstride : k_row * L + 4,
-                            KHALF, 32, CU_TENSOR_MAP_SWIZZLE_128B, "ko_attention_f32 k");
-  if (rc) return rc;
-  // query tiles in pairs (clusters of two along x); an odd count gets one tile of padding rows
+  // Work items: query tiles in pairs (an odd count gets one tile of padding rows) x heads x batch items, spread
+  // over as many CTA pairs (clusters of two) as the GPU holds at once; each pair loops over its items.
   const int64_t qtiles = (L + BQ - 1) / BQ;
-  dim3 grid(static_cast<unsigned>((qtiles + 1) & ~int64_t(1)), static_cast<unsigned>(heads),
-            static_cast<unsigned>(batch));
+  const int64_t pairs = (qtiles + 1) / 2, total = pairs * heads * batch;
+  if (total > INT32_MAX) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": too many query tiles");
+  a.heads = static_cast<int>(heads);
+  a.pairs = static_cast<int>(pairs);
+  a.total_items = static_cast<int>(total);
   const ko::DeviceInfo* dinfo = nullptr;
   rc = ko::device_or_fail(&dinfo, who);
   if (rc) return rc;
@@ -711,28 +748,41 @@ extern "C" int ko_attention_f32(const float* q, const float* k, const float* v, 
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  // Resident CTA pairs (one CTA per SM: shared and tensor memory), found once per device and head dim by the
+  // occupancy calculator; the grid is that many pairs or the item count, whichever is smaller.
+  static int max_clusters_dev[16][2] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) dev = 0;
+  int* max_clusters = max_clusters_dev[dev];
+  auto launch = [&](auto kernel, size_t smem_bytes, int slot) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem_bytes));
+    if (e != cudaSuccess) return e;
+    cfg.dynamicSmemBytes = smem_bytes;
+    if (max_clusters[slot] <= 0) {
+      cfg.gridDim = dim3(2 * static_cast<unsigned>(info.sm_count / 2));
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+      if (e != cudaSuccess) return e;
+      max_clusters[slot] = n > 0 ? n : 1;
+    }
+    a.n_clusters = static_cast<int>(std::min<int64_t>(total, max_clusters[slot]));
+    cfg.gridDim = dim3(2 * static_cast<unsigned>(a.n_clusters));
+    return cudaLaunchKernelEx(&cfg, kernel, mq, a);
+  };
   cudaError_t e;
   if (head_dim == 64) {
     using C = AttnCfg<64>;
     if (static_cast<int64_t>(C::kSmemBytes) > info.max_smem_optin)
       return ko::fail(KO_ERR_UNSUPPORTED, std::string(who) + ": not enough shared memory on this device");
-    e = cudaFuncSetAttribute(attention_tf32x3_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(C::kSmemBytes));
-    if (e != cudaSuccess) return ko::fail(static_cast<int>(e), std::string(who) + ": cudaFuncSetAttribute failed");
-    cfg.dynamicSmemBytes = C::kSmemBytes;
-    e = cudaLaunchKernelEx(&cfg, attention_tf32x3_kernel<64>, mq, mk, a);
+    e = launch(attention_tf32x3_kernel<64>, C::kSmemBytes, 0);
   } else {
     using C = AttnCfg<32>;
-    e = cudaFuncSetAttribute(attention_tf32x3_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(C::kSmemBytes));
-    if (e != cudaSuccess) return ko::fail(static_cast<int>(e), std::string(who) + ": cudaFuncSetAttribute failed");
-    cfg.dynamicSmemBytes = C::kSmemBytes;
-    e = cudaLaunchKernelEx(&cfg, attention_tf32x3_kernel<32>, mq, mk, a);
+    e = launch(attention_tf32x3_kernel<32>, C::kSmemBytes, 1);
   }
   if (e != cudaSuccess) return ko::fail(static_cast<int>(e), std::string(who) + ": launch failed");
   return ko::check_launch(who);

@@ -21,9 +21,10 @@
 // 401-token window: four key blocks) does not pay a whole CTA prologue per item. The pair runs the 5th-generation
 // tensor cores of two SMs as one (tcgen05 cta_group::2): every MMA has M = 256, rows 0-127 being the leader's
 // (rank 0) query tile and 128-255 the peer's, each CTA holding its own A rows and HALF of B at the same
-// shared-memory offset and receiving its 128 rows of the product in its own tensor memory. So each SM loads, splits and stores only half of each k / v tile, and its tensor core reads only half of
-// each B operand; and the halves fit twice in shared memory, so the loaders write block j + 1 while block j's
-// MMAs read block j (with one buffer, each block's k and v writes waited for the previous block's MMAs).
+// shared-memory offset and receiving its 128 rows of the product in its own tensor memory. So each SM loads,
+// splits and stores only half of each k / v tile, and its tensor core reads only half of each B operand; and the
+// halves fit twice in shared memory, so the loaders write block j + 1 while block j's MMAs read block j (with
+// one buffer, each block's k and v writes waited for the previous block's MMAs).
 //   warp 0      allocates the pair's tensor memory; in the leader, one lane issues the MMAs of both CTAs:
 //                 S  = Q K_j^T      (M 256, N = 128 keys, K = head dim;  A, B in shared memory)
 //                 O_j = P_j V_j     (M 256, N = head dim, K = 128 keys; A = P in tensor memory, B in shared)

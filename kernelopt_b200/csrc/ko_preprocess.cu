@@ -7,11 +7,18 @@
 //
 // B200 design: every thread produces 4 consecutive outputs and writes them with one 128-bit store, from source
 // rows staged in shared memory with 16-byte copies, so both the row reads and the output writes are fully
-// coalesced. Outputs up to 682 wide (the model's 640) use the band kernel: one CTA per band of output rows, with
-// the x taps in registers, the LUT in shared memory and the next row pair prefetched with cp.async into a ring of
-// three buffers while the current one is computed. Wider outputs use one CTA per output row. All images of a batch (any sizes) go in one
-// launch. Three output layouts share the kernel: HWC (the reference's), CHW (NCHW batches) and PATCH16 (the
-// im2col of the ViT 16x16 patch embedding, which turns that convolution into a plain GEMM).
+// coalesced. Three kernels share that scheme:
+//   - the segment kernel (640-wide HWC / PATCH16 outputs from 16-byte aligned rows: the model's case): persistent
+//     warps, each working alone on (image, 16-row band, 128-element segment) tasks with its own cp.async ring of
+//     source-row windows; no CTA-wide barrier. Where the right-hand x tap has weight zero everywhere in a segment
+//     (1920 -> 640, an exact 3:1 ratio, in both table modes) it loads and weighs the left taps only.
+//   - the band kernel (other outputs up to 682 wide, CHW, unaligned rows): one CTA per band of output rows with
+//     the x taps in registers, the LUT in shared memory and the next row pair prefetched with cp.async into a
+//     ring of three buffers while the current one is computed;
+//   - one CTA per output row for wider outputs.
+// All images of a batch (any sizes) go in one launch. Three output layouts share the kernels: HWC (the
+// reference's), CHW (NCHW batches) and PATCH16 (the im2col of the ViT 16x16 patch embedding, which turns that
+// convolution into a plain GEMM).
 #include <cstring>
 #include <type_traits>
 
@@ -312,6 +319,221 @@ __global__ void __launch_bounds__(kBandThreads, kBandThreads <= 256 ? 3 : 2) pre
     rows(std::integral_constant<int, 1>{});
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// Segment kernel (640-wide outputs from 16-byte aligned sources: the model's case). Every warp works alone:
+// no CTA-wide barrier after the LUT is loaded.
+//
+// A task is (image, band of kSegBand output rows, segment of 32 float4 items = 128 output elements). Warps are
+// persistent and take tasks round-robin, so the 15 segments of a band run at the same time on neighbouring
+// warps and each source row comes from HBM once. For a task the warp loads its lanes' taps, reduces them to the
+// byte window of a source row that the segment reads (about 400 bytes for a 1920-pixel row) and walks the band:
+// the windows of the two source rows of row y + kSegAhead are copied with 16-byte cp.async into the warp's own
+// ring of kSegBufs row-pair slots while row y is computed from its slot; the rows' ytab entries ride along in
+// registers a row ahead of their use. cp.async.wait_group and __syncwarp are the only waits. A window wider than
+// a slot (tables this kernel was not sized for) makes the warp read that task's taps from global memory instead.
+// ---------------------------------------------------------------------------------------------------------
+constexpr int kSegDst = 640;
+constexpr int kSegItems = kSegDst * 3 / 4;        // float4 items per output row
+constexpr int kSegPerRow = kSegItems / 32;        // segments per output row
+constexpr int kSegWarps = 8;
+constexpr int kSegBand = 16;                      // output rows per task
+constexpr int kSegWin = 512;                      // bytes of a staged source-row window
+constexpr int kSegBufs = 4;
+constexpr int kSegAhead = kSegBufs - 2;
+constexpr int kSegSmem = 768 * 4 + kSegWarps * kSegBufs * 2 * kSegWin;
+static_assert(kSegItems % 32 == 0 && kSegDst % kSegBand == 0 && kSegBand % kSegBufs == 0, "segment tiling");
+
+template <int MODE>
+__device__ __forceinline__ int seg_value(int A, int B, int C, int D, int4 t, int yz, int yw) {
+  int q;
+  if (MODE == 0) {
+    const int left = (A * 256 + (C - A) * yz + 128) >> 8;
+    const int right = (B * 256 + (D - B) * yz + 128) >> 8;
+    q = (left * 256 + (right - left) * t.z + 128) >> 8;
+  } else {
+    const int h0 = A * t.z + B * t.w;
+    const int h1 = C * t.z + D * t.w;
+    q = ((((h0 >> 4) * yz) >> 16) + (((h1 >> 4) * yw) >> 16) + 2) >> 2;
+  }
+  return min(max(q, 0), 255);
+}
+
+// The same value when the right-hand x tap has weight zero (t.w == 0 in mode 1, t.z == 0 in mode 0): exactly
+// the full formula with B = D = anything, without their loads and products. 1920-pixel rows resized to 640 (an
+// exact 3:1 ratio) have such tables in both modes.
+template <int MODE>
+__device__ __forceinline__ int seg_value_left(int A, int C, int4 t, int yz, int yw) {
+  int q;
+  if (MODE == 0) {
+    q = (A * 256 + (C - A) * yz + 128) >> 8;
+  } else {
+    q = ((((A * t.z) >> 4) * yz >> 16) + (((C * t.z) >> 4) * yw >> 16) + 2) >> 2;
+  }
+  return min(max(q, 0), 255);
+}
+
+__global__ void __launch_bounds__(kSegWarps * 32, 4) preprocess_seg_kernel(const __grid_constant__ BatchParams p,
+                                                                           const float* __restrict__ lut,
+                                                                           int layout, float* __restrict__ out,
+                                                                           int n_tasks) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  float* slut = reinterpret_cast<float*>(smem);  // [3][256]
+  for (int i = threadIdx.x; i < 768; i += blockDim.x) slut[i] = __ldg(lut + i);
+  __syncthreads();  // the only CTA-wide barrier: the LUT is in place
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ring = smem + 768 * 4 + warp * kSegBufs * 2 * kSegWin;  // [kSegBufs][2][kSegWin]
+  constexpr int bands = kSegDst / kSegBand;
+  const int n_warps = gridDim.x * kSegWarps;
+
+  for (int task = blockIdx.x * kSegWarps + warp; task < n_tasks; task += n_warps) {
+    const int seg = task % kSegPerRow;
+    const int band = (task / kSegPerRow) % bands;
+    const int image = task / (kSegPerRow * bands);
+    const ImageParams& im = p.img[image];
+    const int item = seg * 32 + lane;
+    const int last = static_cast<int>(im.src_w) * 3 - 1;
+    const int rmax = static_cast<int>(im.src_h) - 1;
+
+    // The item's taps (as in the band kernel) and the segment's source window [wlo, whi).
+    int4 tap[4];
+    int lut_off[4];
+    int64_t col_off;
+    if (layout == KO_LAYOUT_CHW) {
+      constexpr int per_ch = kSegDst / 4;
+      const int c_rgb = item / per_ch, x0 = (item - c_rgb * per_ch) * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        tap[j] = __ldg(im.xtab + (x0 + j) * 3 + (2 - c_rgb));
+        lut_off[j] = c_rgb << 8;
+      }
+      col_off = static_cast<int64_t>(c_rgb) * kSegDst * kSegDst + x0;
+    } else {
+      const int o0 = item * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int o = o0 + j, x = o / 3, c_rgb = o - x * 3;
+        tap[j] = __ldg(im.xtab + x * 3 + (2 - c_rgb));
+        lut_off[j] = c_rgb << 8;
+      }
+      if (layout == KO_LAYOUT_HWC) {
+        col_off = o0;
+      } else {
+        const int px = o0 / 48;
+        col_off = static_cast<int64_t>(px) * 768 + (o0 - px * 48);
+      }
+    }
+    int lo = last, hi = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      tap[j].x = min(max(tap[j].x, 0), last);
+      tap[j].y = min(max(tap[j].y, 0), last);
+      lo = min(lo, min(tap[j].x, tap[j].y));
+      hi = max(hi, max(tap[j].x, tap[j].y));
+    }
+    lo = __reduce_min_sync(0xffffffffu, lo);
+    hi = __reduce_max_sync(0xffffffffu, hi);
+    const int wlo = lo & ~15;
+    const int whi = min((hi + 16) & ~15, last + 1);  // rows are whole 16-byte chunks (vec_ok)
+    const int n16 = (whi - wlo) >> 4;
+    float* obase = out + static_cast<int64_t>(image) * kSegDst * kSegDst * 3 + col_off;
+    const int y0 = band * kSegBand;
+
+    if (whi - wlo > kSegWin) {  // window wider than a slot: taps straight from global memory
+      for (int y = y0; y < y0 + kSegBand; ++y) {
+        const int4 yt = __ldg(im.ytab + y);
+        const uint8_t* top = im.src + static_cast<int64_t>(min(max(yt.x, 0), rmax)) * im.src_stride;
+        const uint8_t* bot = im.src + static_cast<int64_t>(min(max(yt.y, 0), rmax)) * im.src_stride;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int4 t = tap[j];
+          const int A = top[t.x], B = top[t.y], C = bot[t.x], D = bot[t.y];
+          const int q =
+              im.mode == 0 ? seg_value<0>(A, B, C, D, t, yt.z, yt.w) : seg_value<1>(A, B, C, D, t, yt.z, yt.w);
+          v[j] = slut[lut_off[j] + q];
+        }
+        *reinterpret_cast<float4*>(obase + row_term(layout, y, kSegDst)) = make_float4(v[0], v[1], v[2], v[3]);
+      }
+      continue;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      tap[j].x -= wlo;
+      tap[j].y -= wlo;
+    }
+    const uint8_t* src = im.src + wlo;
+    const int64_t stride = im.src_stride;
+
+    // Copy the two source windows of output row y into slot `buf` (n16 <= 32 chunks per window: one per lane).
+    auto stage = [&](int y, int4 yt, int buf) {
+      if (y < y0 + kSegBand && lane < n16) {
+        uint8_t* s = ring + buf * 2 * kSegWin + 16 * lane;
+        cp_async16(s, src + static_cast<int64_t>(min(max(yt.x, 0), rmax)) * stride + 16 * lane);
+        cp_async16(s + kSegWin, src + static_cast<int64_t>(min(max(yt.y, 0), rmax)) * stride + 16 * lane);
+      }
+      cp_async_commit();
+    };
+    // ytab entries: rows y (weights), y + 1, and y + kSegAhead (its copies are issued at step y).
+    int4 yt0 = __ldg(im.ytab + y0), yt1 = __ldg(im.ytab + y0 + 1);
+    int4 yt2 = __ldg(im.ytab + y0 + kSegAhead);
+    static_assert(kSegAhead == 2, "the ytab register ring holds rows y .. y + 2");
+    stage(y0, yt0, 0);
+    stage(y0 + 1, yt1, 1);
+
+    auto rows = [&](auto mode_c, auto left_c) {
+      constexpr int MODE = decltype(mode_c)::value;
+      constexpr bool LEFT = decltype(left_c)::value;
+      int y = y0;
+      auto step = [&](auto buf_c) {
+        constexpr int BUF = decltype(buf_c)::value;
+        stage(y + kSegAhead, yt2, (BUF + kSegAhead) % kSegBufs);
+        const int yz = yt0.z, yw = yt0.w;
+        yt0 = yt1;
+        yt1 = yt2;
+        yt2 = __ldg(im.ytab + min(y + kSegAhead + 1, kSegDst - 1));
+        asm volatile("cp.async.wait_group %0;" ::"n"(kSegAhead) : "memory");
+        __syncwarp();
+        const uint8_t* s = ring + BUF * 2 * kSegWin;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int4 t = tap[j];
+          const int q = LEFT ? seg_value_left<MODE>(s[t.x], s[kSegWin + t.x], t, yz, yw)
+                             : seg_value<MODE>(s[t.x], s[t.y], s[kSegWin + t.x], s[kSegWin + t.y], t, yz, yw);
+          v[j] = slut[lut_off[j] + q];
+        }
+        *reinterpret_cast<float4*>(obase + row_term(layout, y, kSegDst)) = make_float4(v[0], v[1], v[2], v[3]);
+        ++y;
+      };
+      for (int k = 0; k < kSegBand / kSegBufs; ++k) {
+        step(std::integral_constant<int, 0>{});
+        step(std::integral_constant<int, 1>{});
+        step(std::integral_constant<int, 2>{});
+        step(std::integral_constant<int, 3>{});
+      }
+    };
+    bool left_only = true;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) left_only = left_only && (im.mode == 0 ? tap[j].z == 0 : tap[j].w == 0);
+    left_only = __all_sync(0xffffffffu, left_only);
+    using F = std::false_type;
+    using T = std::true_type;
+    if (im.mode == 0) {
+      if (left_only)
+        rows(std::integral_constant<int, 0>{}, T{});
+      else
+        rows(std::integral_constant<int, 0>{}, F{});
+    } else {
+      if (left_only)
+        rows(std::integral_constant<int, 1>{}, T{});
+      else
+        rows(std::integral_constant<int, 1>{}, F{});
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // the next task refills the slots
+    __syncwarp();
+  }
+}
+
 int validate_image(const ko_image_desc& d, int64_t dst, const char* who) {
   if (!d.src || !d.xtab || !d.ytab) return ko::fail(KO_ERR_INVALID_ARGUMENT, std::string(who) + ": null pointer");
   if (d.src_h < 1 || d.src_w < 1 || d.src_stride < d.src_w * 3 || d.src_w > (1 << 20) || d.src_h > (1 << 20))
@@ -357,6 +579,22 @@ extern "C" int ko_preprocess_batch(const ko_image_desc* images, int n, const flo
   const ko::DeviceInfo& info = *dinfo;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int64_t n_items = dst * 3 / 4;
+  bool seg_ok = dst == kSegDst && layout != KO_LAYOUT_CHW;  // CHW items span 4 pixels of one channel: wide windows
+  for (int i = 0; i < n && seg_ok; ++i) seg_ok = p.img[i].vec_ok;
+  if (seg_ok) {
+    cudaError_t e = cudaFuncSetAttribute(preprocess_seg_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return ko::fail(static_cast<int>(e), "ko_preprocess: cannot set the shared-memory carveout");
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, preprocess_seg_kernel, kSegWarps * 32, kSegSmem);
+    if (e != cudaSuccess || per_sm < 1) return ko::fail(KO_ERR_UNSUPPORTED, "ko_preprocess: segment kernel does not fit");
+    const int n_tasks = n * (kSegDst / kSegBand) * kSegPerRow;
+    const int64_t grid = std::min<int64_t>(static_cast<int64_t>(per_sm) * info.sm_count,
+                                           (n_tasks + kSegWarps - 1) / kSegWarps);
+    preprocess_seg_kernel<<<static_cast<unsigned>(grid), kSegWarps * 32, kSegSmem, st>>>(p, lut, layout, out,
+                                                                                         n_tasks);
+    return ko::check_launch("ko_preprocess");
+  }
   if (n_items <= 2 * kBandThreads) {
     // Band kernel: the largest band (rows per CTA) that still gives every SM about eight CTAs.
     const int64_t target = 8 * static_cast<int64_t>(info.sm_count);

@@ -108,6 +108,25 @@ def test_preprocess_many_frames_use_row_bands(cuda):
     assert np.array_equal(out.cpu().numpy().view(np.uint32), np.stack(refs).view(np.uint32))
 
 
+@pytest.mark.parametrize("policy", ["reference", "opencv"])
+@pytest.mark.parametrize("layout", ["hwc", "patch16"])
+def test_preprocess_many_aligned_frames(cuda, policy, layout):
+    """24 frames whose rows are whole 16-byte chunks (the segment kernel): each warp takes several tasks, crosses
+    images of different sizes and table modes, and runs both the left-tap and the four-tap arithmetic."""
+    lut = gpu_lut(cuda)
+    sizes = [(1080, 1920), (720, 1280), (540, 960), (1080, 1152)]
+    items, refs = [], []
+    for i in range(24):
+        h, w = sizes[i % 4]
+        img = frame(h, w, 300 + i, "noise" if i % 3 else "gradient")
+        mode, xt, yt = RT.tables(w, h, policy=policy)
+        items.append((torch.from_numpy(img).to(cuda), torch.from_numpy(np.array(xt)).to(cuda),
+                      torch.from_numpy(np.array(yt)).to(cuda), mode))
+        refs.append(OR.preprocess(img, policy=policy, layout=layout))
+    out = K.preprocess_batch(items, lut, layout=layout)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), np.stack(refs).view(np.uint32))
+
+
 @pytest.mark.parametrize("hw,dst,policy", [((1080, 1920), 96, "opencv"), ((500, 333), 160, "reference"),
                                            ((1080, 1920), 1024, "reference"), ((1080, 1920), 1024, "opencv"),
                                            ((500, 333), 1024, "reference")])

@@ -17,6 +17,9 @@ frames and D2H copy of its outputs inside the timed region (pipelined: step i+1'
 order inside the timed region (total work fixed: strong scaling). Both arms preprocess with OpenCV's
 fixed-point arithmetic (resize_policy="opencv"), which is bit-exact with the x86-64 cv2.resize the CPU arm calls.
 
+`configs` (rank 0 of a one-GPU run; --no-configs skips it) times the four kernels of configs 1-4 on their own at
+each of their batch sizes, with a cold L2 (kernelopt_b200.profile_kernels' workloads).
+
 --impl reference times the reference's CPU path on the host cores instead: cv2.resize + numpy normalisation and
 the reference's unfused RF-DETR graph restated in torch-CPU fp32 (the oracle; MLX itself cannot be installed
 here), one frame per step, rank 0 only.
@@ -180,6 +183,55 @@ def instrumented_step(det, runner_x, items, K):
         secs, work, cnt = t.total()
         out[n] = (secs, work, cnt, "flop" if n in ("gemm_tf32x3", "gemm_residual_ln", "attention_tf32x3") else "byte")
     return out, launches
+
+
+# Configs 1-4 (the four kernels at their own sizes): (profile_kernels workload, batch sizes). Config 1's B=3 is the
+# three frame sizes in one launch; config 4 samples the decoder's fused [B, 1600, 1024] value layout.
+CONFIG_RUNS = (("preprocess", "preprocess", (1, 3, 64)), ("residual_layernorm", "resln", (1, 3, 64)),
+               ("linear_gelu_f32", "gemm", (1, 3, 32)), ("deform_attn", "deform_model", (1, 3, 64)))
+
+
+def config_runs(dev, iters: int = 10) -> dict:
+    """CUDA-event time of each kernel at its config's batch sizes, cold L2 (a 256 MB write + read-back before
+    every timed launch), the host held off by a spin kernel; median of `iters`."""
+    import torch
+
+    from kernelopt_b200.benchutil import hold_stream, measured_peaks
+    from kernelopt_b200.profile_kernels import setup
+
+    peaks = measured_peaks()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    res = {}
+    for name, kernel, batches in CONFIG_RUNS:
+        res[name] = {}
+        for b in batches:
+            fn, work, unit = setup(kernel, b, dev)
+            for _ in range(3):
+                fn()
+            ts = []
+            for _ in range(iters):
+                flush.fill_(1.0)
+                flush.sum()
+                hold_stream(0.002)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1) / 1e3)
+            t = statistics.median(ts)
+            if unit == "flop":
+                ach, peak, u = work / t / 1e12, peaks["bf16_tflops"] / 6.0, "TFLOP/s"
+            else:
+                ach, peak, u = work / t / 1e9, peaks["hbm_gbs"], "GB/s"
+            res[name][str(b)] = {"us": t * 1e6, "achieved": ach, "unit": u, "frac": ach / peak}
+            del fn
+    del flush
+    torch.cuda.empty_cache()
+    res["note"] = ("configs 1-4 at their batch sizes (1 = 1080p, 3 = 1080p + 720p + 540p, 64 = 64 frames cycling "
+                   "those sizes for preprocessing); cold L2, median of %d launches; fractions of the measured HBM "
+                   "copy bandwidth or of the 3xTF32 ceiling (measured bf16 / 6)" % iters)
+    return res
 
 
 def run_ours(args, rank: int, world: int):
@@ -358,6 +410,8 @@ def run_ours(args, rank: int, world: int):
             "roofline": roofline, "kernels": kernels, "clocks": clk.summary(),
             "latency_ms": dict(latency, note="median CUDA-event time of preprocessing + forward for one batch, "
                                              "frames resident on the device")}
+    if rank == 0 and world == 1 and not args.no_configs:
+        line["configs"] = config_runs(dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         fps, n, cores = cpu_reference_run(10_000, budget_s=args.cpu_seconds)
         line["cpu_baseline"] = {"value": fps, "unit": "frames/s", "cores": cores, "kind": "port",
@@ -382,6 +436,7 @@ def main():
     ap.add_argument("--stream-frames", type=int, default=512,
                     help="frames of the sharded stream measurement (0 skips it)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the per-config kernel timings (configs 1-4)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

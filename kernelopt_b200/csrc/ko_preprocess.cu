@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(kBandThreads, kBandThreads <= 256 ? 3 : 2) pre
 // Segment kernel (640-wide outputs from 16-byte aligned sources: the model's case). Every warp works alone:
 // no CTA-wide barrier after the LUT is loaded.
 //
-// A task is (image, band of kSegBand output rows, segment of 32 float4 items = 128 output elements). Warps are
+// A task is (image, band of 4-16 output rows, segment of 32 float4 items = 128 output elements). Warps are
 // persistent and take tasks round-robin, so the 15 segments of a band run at the same time on neighbouring
 // warps and each source row comes from HBM once. For a task the warp loads its lanes' taps, reduces them to the
 // byte window of a source row that the segment reads (about 400 bytes for a 1920-pixel row) and walks the band:
@@ -336,12 +336,12 @@ constexpr int kSegDst = 640;
 constexpr int kSegItems = kSegDst * 3 / 4;        // float4 items per output row
 constexpr int kSegPerRow = kSegItems / 32;        // segments per output row
 constexpr int kSegWarps = 8;
-constexpr int kSegBand = 16;                      // output rows per task
+constexpr int kSegBandMax = 16;                   // output rows per task (4, 8 or 16: fewer for small batches)
 constexpr int kSegWin = 512;                      // bytes of a staged source-row window
 constexpr int kSegBufs = 4;
 constexpr int kSegAhead = kSegBufs - 2;
 constexpr int kSegSmem = 768 * 4 + kSegWarps * kSegBufs * 2 * kSegWin;
-static_assert(kSegItems % 32 == 0 && kSegDst % kSegBand == 0 && kSegBand % kSegBufs == 0, "segment tiling");
+static_assert(kSegItems % 32 == 0 && kSegDst % kSegBandMax == 0 && kSegBandMax % kSegBufs == 0, "segment tiling");
 
 template <int MODE>
 __device__ __forceinline__ int seg_value(int A, int B, int C, int D, int4 t, int yz, int yw) {
@@ -375,14 +375,14 @@ __device__ __forceinline__ int seg_value_left(int A, int C, int4 t, int yz, int 
 __global__ void __launch_bounds__(kSegWarps * 32, 4) preprocess_seg_kernel(const __grid_constant__ BatchParams p,
                                                                            const float* __restrict__ lut,
                                                                            int layout, float* __restrict__ out,
-                                                                           int n_tasks) {
+                                                                           int n_tasks, int band_rows) {
   extern __shared__ __align__(16) uint8_t smem[];
   float* slut = reinterpret_cast<float*>(smem);  // [3][256]
   for (int i = threadIdx.x; i < 768; i += blockDim.x) slut[i] = __ldg(lut + i);
   __syncthreads();  // the only CTA-wide barrier: the LUT is in place
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* ring = smem + 768 * 4 + warp * kSegBufs * 2 * kSegWin;  // [kSegBufs][2][kSegWin]
-  constexpr int bands = kSegDst / kSegBand;
+  const int bands = kSegDst / band_rows;
   const int n_warps = gridDim.x * kSegWarps;
 
   for (int task = blockIdx.x * kSegWarps + warp; task < n_tasks; task += n_warps) {
@@ -436,10 +436,10 @@ __global__ void __launch_bounds__(kSegWarps * 32, 4) preprocess_seg_kernel(const
     const int whi = min((hi + 16) & ~15, last + 1);  // rows are whole 16-byte chunks (vec_ok)
     const int n16 = (whi - wlo) >> 4;
     float* obase = out + static_cast<int64_t>(image) * kSegDst * kSegDst * 3 + col_off;
-    const int y0 = band * kSegBand;
+    const int y0 = band * band_rows;
 
     if (whi - wlo > kSegWin) {  // window wider than a slot: taps straight from global memory
-      for (int y = y0; y < y0 + kSegBand; ++y) {
+      for (int y = y0; y < y0 + band_rows; ++y) {
         const int4 yt = __ldg(im.ytab + y);
         const uint8_t* top = im.src + static_cast<int64_t>(min(max(yt.x, 0), rmax)) * im.src_stride;
         const uint8_t* bot = im.src + static_cast<int64_t>(min(max(yt.y, 0), rmax)) * im.src_stride;
@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(kSegWarps * 32, 4) preprocess_seg_kernel(const
 
     // Copy the two source windows of output row y into slot `buf` (n16 <= 32 chunks per window: one per lane).
     auto stage = [&](int y, int4 yt, int buf) {
-      if (y < y0 + kSegBand && lane < n16) {
+      if (y < y0 + band_rows && lane < n16) {
         uint8_t* s = ring + buf * 2 * kSegWin + 16 * lane;
         cp_async16(s, src + static_cast<int64_t>(min(max(yt.x, 0), rmax)) * stride + 16 * lane);
         cp_async16(s + kSegWin, src + static_cast<int64_t>(min(max(yt.y, 0), rmax)) * stride + 16 * lane);
@@ -505,7 +505,7 @@ __global__ void __launch_bounds__(kSegWarps * 32, 4) preprocess_seg_kernel(const
         *reinterpret_cast<float4*>(obase + row_term(layout, y, kSegDst)) = make_float4(v[0], v[1], v[2], v[3]);
         ++y;
       };
-      for (int k = 0; k < kSegBand / kSegBufs; ++k) {
+      for (int k = 0; k < band_rows / kSegBufs; ++k) {
         step(std::integral_constant<int, 0>{});
         step(std::integral_constant<int, 1>{});
         step(std::integral_constant<int, 2>{});
@@ -588,11 +588,16 @@ extern "C" int ko_preprocess_batch(const ko_image_desc* images, int n, const flo
     int per_sm = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, preprocess_seg_kernel, kSegWarps * 32, kSegSmem);
     if (e != cudaSuccess || per_sm < 1) return ko::fail(KO_ERR_UNSUPPORTED, "ko_preprocess: segment kernel does not fit");
-    const int n_tasks = n * (kSegDst / kSegBand) * kSegPerRow;
+    // Bands of 16 rows, or 8 / 4 when the batch is too small to give every resident warp two tasks.
+    int band_rows = kSegBandMax;
+    while (band_rows > kSegBufs &&
+           static_cast<int64_t>(n) * (kSegDst / band_rows) * kSegPerRow < 2LL * per_sm * info.sm_count * kSegWarps)
+      band_rows /= 2;
+    const int n_tasks = n * (kSegDst / band_rows) * kSegPerRow;
     const int64_t grid = std::min<int64_t>(static_cast<int64_t>(per_sm) * info.sm_count,
                                            (n_tasks + kSegWarps - 1) / kSegWarps);
     preprocess_seg_kernel<<<static_cast<unsigned>(grid), kSegWarps * 32, kSegSmem, st>>>(p, lut, layout, out,
-                                                                                         n_tasks);
+                                                                                         n_tasks, band_rows);
     return ko::check_launch("ko_preprocess");
   }
   if (n_items <= 2 * kBandThreads) {

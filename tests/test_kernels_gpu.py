@@ -110,13 +110,15 @@ def test_preprocess_many_frames_use_row_bands(cuda):
 
 @pytest.mark.parametrize("policy", ["reference", "opencv"])
 @pytest.mark.parametrize("layout", ["hwc", "patch16"])
-def test_preprocess_many_aligned_frames(cuda, policy, layout):
-    """24 frames whose rows are whole 16-byte chunks (the segment kernel): each warp takes several tasks, crosses
-    images of different sizes and table modes, and runs both the left-tap and the four-tap arithmetic."""
+@pytest.mark.parametrize("n_frames", [10, 24])
+def test_preprocess_many_aligned_frames(cuda, policy, layout, n_frames):
+    """Frames whose rows are whole 16-byte chunks (the segment kernel; 10 frames take 8-row bands, 24 take 16-row
+    bands): each warp takes several tasks, crosses images of different sizes and table modes, and runs both the
+    left-tap and the four-tap arithmetic."""
     lut = gpu_lut(cuda)
     sizes = [(1080, 1920), (720, 1280), (540, 960), (1080, 1152)]
     items, refs = [], []
-    for i in range(24):
+    for i in range(n_frames):
         h, w = sizes[i % 4]
         img = frame(h, w, 300 + i, "noise" if i % 3 else "gradient")
         mode, xt, yt = RT.tables(w, h, policy=policy)

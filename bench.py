@@ -314,12 +314,17 @@ def run_ours(args, rank: int, world: int):
         def batch_at(s, e):   # the stream's frames cycle through this rank's B pinned frames
             return host[:e - s]
 
+        # A rank's shard goes through detect_stream in batches of B, or in four smaller ones (at least 8 frames)
+        # when the shard is shorter than 4 B: a one-batch shard could not overlap its copy-in with any compute.
+        per_rank = -(-args.stream_frames // world)
+        sb = B if per_rank >= 4 * B else max(8, per_rank // 4)
+
         def run_stream():
             if world == 1:
-                outs = list(det.detect_stream(batch_at(s, min(s + B, args.stream_frames))
-                                              for s in range(0, args.stream_frames, B)))
+                outs = list(det.detect_stream(batch_at(s, min(s + sb, args.stream_frames))
+                                              for s in range(0, args.stream_frames, sb)))
                 return np.concatenate([o[0] for o in outs]), np.concatenate([o[1] for o in outs])
-            return run_sharded_stream(det.detect_stream, batch_at, args.stream_frames, B)
+            return run_sharded_stream(det.detect_stream, batch_at, args.stream_frames, sb)
 
         run_stream()                                            # warm-up (and the gather's first use)
         torch.cuda.synchronize()
@@ -344,9 +349,9 @@ def run_ours(args, rank: int, world: int):
         n_mine = len(shard_range(args.stream_frames, rank, world))
         stream_line = {"frames": args.stream_frames, "value": args.stream_frames / st_secs, "unit": "frames/s",
                        "seconds": st_secs, "scaling": "strong", "frames_per_rank": n_mine,
-                       "h2d_gbs_per_rank_min": h2d_min,
+                       "h2d_gbs_per_rank_min": h2d_min, "batch": sb,
                        "path": "run_sharded_stream: detect_stream over the rank's shard in batches of "
-                               f"{B} from pinned host frames, outputs gathered on rank 0 in stream order",
+                               f"{sb} from pinned host frames, outputs gathered on rank 0 in stream order",
                        "time": "host wall clock from a barrier to the gathered outputs, max over ranks"}
         barrier()
 

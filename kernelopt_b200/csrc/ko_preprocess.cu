@@ -9,7 +9,7 @@
 // rows staged in shared memory with 16-byte copies, so both the row reads and the output writes are fully
 // coalesced. Three kernels share that scheme:
 //   - the segment kernel (640-wide HWC / PATCH16 outputs from 16-byte aligned rows: the model's case): persistent
-//     warps, each working alone on (image, 16-row band, 128-element segment) tasks with its own cp.async ring of
+//     warps, each working alone on (image, band of 4-16 rows, 128-element segment) tasks with its own cp.async ring of
 //     source-row windows; no CTA-wide barrier. Where the right-hand x tap has weight zero everywhere in a segment
 //     (1920 -> 640, an exact 3:1 ratio, in both table modes) it loads and weighs the left taps only.
 //   - the band kernel (other outputs up to 682 wide, CHW, unaligned rows): one CTA per band of output rows with

@@ -48,7 +48,7 @@ WORKLOAD = ("RF-DETR-Medium fp32 inference on seeded 1920x1080 uint8 BGR frames:
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --clock-control none
 #       -k regex:gemm_tf32x3 -s 1 -c 1 python -m kernelopt_b200.profile_kernels --kernel gemm --batch 32 \
 #       --iters 1 --warmup 1                                    (and --kernel qkv)
-# (table and derivation: profiles/gemm_tf32x3_traffic_per_shape.md).
+# The reads of those captures equal the algorithmic reads; the shortfall is output still in L2 at kernel exit.
 GEMM_TRAFFIC_PER_LAUNCH = {64: 376.8e6}
 
 

@@ -44,7 +44,9 @@ def test_sine_embed(cuda, rows):
 
 
 @pytest.mark.parametrize("m,k,n,act", [(19200, 256, 11, None), (102400, 256, 11, None), (300, 256, 4, None),
-                                       (7, 256, 11, "relu"), (1, 100, 32, None), (333, 48, 17, "relu")])
+                                       (7, 256, 11, "relu"), (1, 100, 32, None), (333, 48, 17, "relu"),
+                                       (5, 256, 16, None), (33, 256, 1, "relu"), (1000, 256, 5, None),
+                                       (64, 256, 20, None)])
 def test_linear_small(cuda, m, k, n, act):
     r = np.random.default_rng(m + k + n)
     x = r.standard_normal((m, k)).astype(np.float32)

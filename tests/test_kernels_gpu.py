@@ -129,6 +129,21 @@ def test_preprocess_many_aligned_frames(cuda, policy, layout, n_frames):
     assert np.array_equal(out.cpu().numpy().view(np.uint32), np.stack(refs).view(np.uint32))
 
 
+def test_preprocess_benchmark_batch(cuda):
+    """The benchmark's own case: 64 noise frames of 1920x1080 with OpenCV tables into PATCH16 (the segment
+    kernel's left-tap path, 16-row bands, several tasks per warp), bit-exact against the oracle."""
+    lut = gpu_lut(cuda)
+    mode, xt, yt = RT.tables(1920, 1080, policy="opencv")
+    xt_d, yt_d = torch.from_numpy(np.array(xt)).to(cuda), torch.from_numpy(np.array(yt)).to(cuda)
+    rng = np.random.default_rng(64)
+    imgs = [rng.integers(0, 256, (1080, 1920, 3), dtype=np.uint8) for _ in range(64)]
+    out = K.preprocess_batch([(torch.from_numpy(im).to(cuda), xt_d, yt_d, mode) for im in imgs], lut,
+                             layout="patch16").cpu().numpy()
+    for i in range(0, 64, 7):  # every seventh frame: spans images at every position in the warps' task order
+        ref = OR.preprocess(imgs[i], policy="opencv", layout="patch16")
+        assert np.array_equal(out[i].view(np.uint32), ref.view(np.uint32)), i
+
+
 @pytest.mark.parametrize("hw,dst,policy", [((1080, 1920), 96, "opencv"), ((500, 333), 160, "reference"),
                                            ((1080, 1920), 1024, "reference"), ((1080, 1920), 1024, "opencv"),
                                            ((500, 333), 1024, "reference")])

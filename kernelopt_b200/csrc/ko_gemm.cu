@@ -64,8 +64,9 @@ constexpr int EPI_LN = 1;
 // Row statistics exchange of the LayerNorm epilogue: per tile parity, the two epilogue warps of a lane
 // quadrant publish (mean, M2) of their half of the row [2][2][128] float2, and the cluster peer's CTA-level
 // (mean, M2) lands in [2][128] float2; two mbarriers count the peer's arrivals, four (one per lane quadrant)
-// the two warps of a pair, and eight (one per epilogue warp) the TMA loads into the warps' staging tiles.
-constexpr uint32_t kLnStatBytes = 2 * 2 * 128 * 8 + 2 * 128 * 8 + 2 * 8 + 4 * 8 + 8 * 8;
+// the two warps of a pair, and eight or sixteen (one per epilogue warp and staging tile) the TMA loads into
+// the warps' staging tiles.
+constexpr uint32_t kLnStatBytes = 2 * 2 * 128 * 8 + 2 * 128 * 8 + 2 * 8 + 4 * 8 + 16 * 8;
 constexpr uint32_t kLnStatRegion = 6400 + 4 * 256 * 4;  // + the CTA's column slice of bias, scale, gamma, beta
 static_assert(kLnStatBytes <= kLnStatRegion, "stat region");
 
@@ -78,7 +79,14 @@ struct Cfg {
   // and only B from shared memory) for 192-wide tiles, where the accumulators leave 128 TMEM columns free.
   static constexpr bool kTSA = BN == 192 && BKB == 64;
   static constexpr uint32_t kStageBytes = (kTSA ? 1 : 2) * kATileBytes + 2 * kBTileBytes;
-  static constexpr uint32_t kStatBytes = EPI == EPI_LN ? kLnStatRegion : 0;
+  // LayerNorm epilogue without the correction accumulator: a second staging tile per epilogue warp (at kStg2Off
+  // from the first set, 1024-byte aligned, after the statistics region), so a chunk's residual load overlaps the
+  // previous chunk and a store's read-back does not hold up the next chunk. With the correction accumulator the
+  // 32 KB would cost fc2 a pipeline stage (measured 593 -> 669 us at 64 frames), so those variants keep one tile.
+  static constexpr int kStgTiles = (EPI == EPI_LN && !SPLIT) ? 2 : 1;
+  static constexpr uint32_t kStg2Off = (kStoreBytes + kBarBytes + kLnStatRegion + 1023) / 1024 * 1024;
+  static constexpr uint32_t kStatBytes =
+      EPI == EPI_LN ? (kStgTiles == 2 ? kStg2Off - kBarBytes : kLnStatRegion) : 0;
   static constexpr int kStagesRaw = static_cast<int>((kSmemBudget - kStatBytes) / kStageBytes);
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   // The A slots form their own ring of 4 (k-block kit uses slot kit % 4), so TMA can run more stages ahead
@@ -280,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&peer_bar[0], 128);  // one arrival per lane of the peer's four first-half epilogue warps
       mbar_init(&peer_bar[1], 128);
       for (int q = 0; q < 4; ++q) mbar_init(&pair_bar[q], 64);  // every thread of the two warps of a quadrant
-      for (int w = 0; w < 8; ++w) mbar_init(&load_bar[w], 1);
+      for (int w = 0; w < 8 * C::kStgTiles; ++w) mbar_init(&load_bar[w], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -571,6 +579,172 @@ __global__ void __launch_bounds__(kThreads, 1)
       lphase ^= 1u;
       return done;
     };
+    if constexpr (C::kStgTiles == 2) {
+      // Two staging tiles per warp (no correction accumulator, so v stays in tensor memory between the passes).
+      // A running chunk count gk picks the tile (gk & 1). Pass 1 issues the next chunk's residual load into the
+      // other tile before it waits for and works on this chunk's, so each residual read overlaps the previous
+      // chunk; before a tile is loaded or written, the bulk stores issued from it have read it (the newest
+      // store may stay pending when it came from the other tile).
+      uint8_t* const stl[2] = {stile, store_smem + C::kStg2Off + ew * kStoreTileBytes};
+      uint64_t* const lbr[2] = {&load_bar[ew], &load_bar[8 + ew]};
+      uint32_t lph[2] = {0u, 0u};
+      uint32_t gk = 0;
+      int newest = -1;  // tile of this warp's newest bulk store (-1: none)
+      auto free_tile = [&](int b) {
+        if (lane == 0) {
+          if (newest == b) bulk_wait_read<0>();
+          else if (newest >= 0) bulk_wait_read<1>();
+        }
+        __syncwarp();
+      };
+      auto load_resid = [&](int b, int col0, int row0) {
+        free_tile(b);
+        fence_proxy_async_smem();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(lbr[b], kStoreTileBytes);
+          tma_load_2d(&map_r, lbr[b], stl[b], col0, row0);
+        }
+      };
+      auto store_tile = [&](const CUtensorMap* map, int b, int col0, int row0) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(map, stl[b], col0, row0);
+          bulk_commit();
+        }
+        newest = b;
+      };
+      constexpr int kChunks = BN / 64;  // this warp's 32-column chunks of a tile (c = half, half + 2, ...)
+      int local = 0;
+      for (int tile = ts.first; tile < num_tiles && ok; tile += ts.step, ++local) {
+        const int as = local % NB;
+        const uint32_t acc_phase = (local / NB) & 1u;
+        if (!mbar_wait(&acc_full[as], acc_phase, abort_flag)) break;
+        tc_fence_after();
+        const int m0 = ts.m0(tile), n0 = ts.n0(tile, BN);
+        const int row0 = m0 + quad * 32;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + as * C::kAccCols;
+        if (args.resid && tile + ts.step < num_tiles) {  // the residual slices of this thread's next row into L2
+          const int64_t nrow = static_cast<int64_t>(ts.m0(tile + ts.step)) + row_t;
+          if (nrow < args.M)
+            for (int c = half; c < BN / 32; c += 2) {
+              const float* p = args.resid + nrow * args.N + n0 + c * 32;
+              asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+              asm volatile("prefetch.global.L2 [%0];" ::"l"(p + 31));
+            }
+        }
+        float2 st = make_float2(0.f, 0.f);  // (mean, M2) of the values seen so far
+        float cnt = 0.f;
+        if (args.resid) load_resid(static_cast<int>(gk & 1u), n0 + half * 32, row0);
+#pragma unroll 1
+        for (int ci = 0; ci < kChunks; ++ci) {
+          const int c = half + 2 * ci;
+          const int col0 = n0 + c * 32;
+          const int b = static_cast<int>(gk & 1u);
+          if (args.resid && ci + 1 < kChunks) load_resid(b ^ 1, col0 + 64, row0);  // the next chunk's residual
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          tmem_ld_wait_regs(r);
+          if (args.resid) {
+            ok = mbar_wait(lbr[b], lph[b], abort_flag);
+            lph[b] ^= 1u;
+            if (!ok) break;
+          } else {
+            free_tile(b);  // v is staged in this tile below
+          }
+          uint8_t* sb = stl[b];
+          float sum = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int col = col0 + 4 * j;
+            float4* slot = reinterpret_cast<float4*>(sb + lane * 128 + ((j ^ (lane & 7)) << 4));
+            const float4 hv = args.resid ? *slot : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 bb = *reinterpret_cast<const float4*>(ln_par + (col - ts.col0));
+            const float4 sc = *reinterpret_cast<const float4*>(ln_par + BN + (col - ts.col0));
+            float4 v;
+            v.x = hv.x + (__uint_as_float(r[4 * j + 0]) + bb.x) * sc.x;
+            v.y = hv.y + (__uint_as_float(r[4 * j + 1]) + bb.y) * sc.y;
+            v.z = hv.z + (__uint_as_float(r[4 * j + 2]) + bb.z) * sc.z;
+            v.w = hv.w + (__uint_as_float(r[4 * j + 3]) + bb.w) * sc.w;
+            r[4 * j + 0] = __float_as_uint(v.x);
+            r[4 * j + 1] = __float_as_uint(v.y);
+            r[4 * j + 2] = __float_as_uint(v.z);
+            r[4 * j + 3] = __float_as_uint(v.w);
+            sum += (v.x + v.y) + (v.z + v.w);
+            if (args.write_v) *slot = v;
+          }
+          const float cm = sum * (1.0f / 32.0f);
+          float m2 = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float d = __uint_as_float(r[j]) - cm;
+            m2 += d * d;
+          }
+          if (cnt == 0.f) {
+            st = make_float2(cm, m2);
+          } else {  // Chan: (cnt values) + (32 values)
+            const float tot = cnt + 32.f;
+            const float d = cm - st.x;
+            st.x += d * (32.f / tot);
+            st.y += m2 + d * d * (cnt * 32.f / tot);
+          }
+          cnt += 32.f;
+          tmem_store_x32(taddr + c * 32, r);
+          if (args.write_v) store_tile(&map_v, b, col0, row0);
+          ++gk;
+        }
+        if (!ok) break;
+        tmem_store_wait();
+        // Combine the two halves of the row (same order in both warps of the pair).
+        const int par = local & 1;
+        pair_stats[(par * 2 + half) * 128 + row_t] = st;
+        mbar_arrive(&pair_bar[quad]);
+        if (!mbar_wait(&pair_bar[quad], local & 1, abort_flag)) break;
+        st = combine_stats(pair_stats[(par * 2 + 0) * 128 + row_t], pair_stats[(par * 2 + 1) * 128 + row_t], n_half);
+        if (clustered) {
+          if (half == 0) {
+            const uint32_t dst = cluster_map(smem_addr(&peer_stats[par * 128 + row_t]), peer);
+            cluster_store_f2(dst, st.x, st.y);
+            mbar_arrive_cluster(cluster_map(smem_addr(&peer_bar[par]), peer));
+          }
+          if (!mbar_wait_cluster(&peer_bar[par], (local >> 1) & 1, abort_flag)) break;
+          const float2 other = peer_stats[par * 128 + row_t];
+          st = rank0 ? combine_stats(st, other, static_cast<float>(BN)) : combine_stats(other, st, static_cast<float>(BN));
+        }
+        const float mean = st.x;
+        const float rstd = 1.0f / sqrtf(st.y * inv_n + args.eps);
+#pragma unroll 1
+        for (int ci = 0; ci < kChunks; ++ci) {
+          const int c = half + 2 * ci;
+          const int col0 = n0 + c * 32;
+          const int b = static_cast<int>(gk & 1u);
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          tmem_ld_wait_regs(r);
+          if (ci + 1 == kChunks) {  // this warp's last read of the tile: release the accumulator
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[as]);
+          }
+          free_tile(b);
+          uint8_t* sb = stl[b];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int col = col0 + 4 * j;
+            const float4 g = *reinterpret_cast<const float4*>(ln_par + 2 * BN + (col - ts.col0));
+            const float4 bt = *reinterpret_cast<const float4*>(ln_par + 3 * BN + (col - ts.col0));
+            float4 o;
+            o.x = ln_act((__uint_as_float(r[4 * j + 0]) - mean) * rstd * g.x + bt.x, args.act);
+            o.y = ln_act((__uint_as_float(r[4 * j + 1]) - mean) * rstd * g.y + bt.y, args.act);
+            o.z = ln_act((__uint_as_float(r[4 * j + 2]) - mean) * rstd * g.z + bt.z, args.act);
+            o.w = ln_act((__uint_as_float(r[4 * j + 3]) - mean) * rstd * g.w + bt.w, args.act);
+            *reinterpret_cast<float4*>(sb + lane * 128 + ((j ^ (lane & 7)) << 4)) = o;
+          }
+          store_tile(&map_out, b, col0, row0);
+          ++gk;
+        }
+      }
+    } else {
     int local = 0;
     for (int tile = ts.first; tile < num_tiles && ok; tile += ts.step, ++local) {
       const int as = local % NB;
@@ -741,6 +915,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           bulk_commit();
         }
       }
+    }
     }
     if (lane == 0) bulk_wait<0>();
     __syncwarp();

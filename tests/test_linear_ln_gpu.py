@@ -69,9 +69,11 @@ def test_linear_residual_ln(cuda, m, k, n):
     assert_close(y, ry, what=f"y {m}x{k}x{n}")
 
 
-@pytest.mark.parametrize("m,k,n", [(1600, 1152, 128), (1600, 768, 256), (1600, 2304, 256)])
+@pytest.mark.parametrize("m,k,n", [(1600, 1152, 128), (1600, 768, 256), (1600, 2304, 256), (1600, 256, 128),
+                                   (3000, 384, 256), (2000, 384, 384)])
 def test_linear_ln_silu_no_residual(cuda, m, k, n):
-    """The projector's conv-as-GEMM -> channel LayerNorm -> SiLU (no residual, no scale, LN eps 1e-6)."""
+    """The projector's conv-as-GEMM -> channel LayerNorm -> SiLU (no residual, no scale, LN eps 1e-6); K <= 512
+    also runs the epilogue with two staging tiles per warp without any residual load or v store."""
     d = make(m, k, n, 7 * n, resid=False, scale=False)
     h_out, y = run(cuda, d, act="silu", write_h=False)
     assert h_out is None
